@@ -1,0 +1,119 @@
+/*
+ * kq_b200.h -- C ABI of the kquant_b200 EXL3/QSRT trellis encoder for B200 (sm_100a).
+ *
+ * Every entry point takes plain device pointers, element counts and a
+ * cudaStream_t (passed as void*).  It never allocates device memory, never
+ * synchronizes the stream, and returns a KQ_* status code (0 on success).
+ * kq_last_error() returns a readable message for the last failure of the
+ * calling host thread.  Outputs and workspaces are caller-allocated, like the
+ * reference extension's (kquant/csrc/sqg_quantize.cu:165-209).
+ *
+ * Layouts:
+ *   tiles        float32 [n_tiles][256], 16x16 tiles already permuted to the
+ *                tensor-core element order that the trellis runs along
+ *                (kquant/exl3_encoder_backend.py:27-50)
+ *   states       uint16  [n_tiles][256], 16-bit trellis state per element
+ *   packed       uint16  [n_tiles][16*K], native EXL word order with SWAP16
+ *   lut          uint8   [65536] E4M3 label bytes indexed by the 16-bit state
+ *                (untransposed; kquant/sqg_e4m3.py:305-333)
+ *   labels       uint16  [65536] binary16 labels indexed by state
+ */
+#ifndef KQ_B200_H
+#define KQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KQ_OK 0
+#define KQ_ERR_ARG (-1)        /* invalid argument (shape, K, context, pointer) */
+#define KQ_ERR_WORKSPACE (-2)  /* workspace too small */
+#define KQ_ERR_CUDA (-3)       /* CUDA runtime error (launch, attribute, device) */
+#define KQ_ERR_ALIGN (-4)      /* pointer not aligned as the kernel requires */
+
+/* Codebook kinds, numbered like the reference's `cb` template argument
+ * (kquant/csrc/qsrt_quantize_tiles_kernel.cuh:21, exl3_compat/quant/codebook.cuh). */
+#define KQ_CB_3INST 0
+#define KQ_CB_MCG 1
+#define KQ_CB_MUL1 2
+#define KQ_CB_SQG 4
+
+/* Message describing the last non-zero status returned on this host thread. */
+const char* kq_last_error(void);
+
+/* ABI version, bumped when a signature changes. */
+int kq_abi_version(void);
+
+/*
+ * Decode a codebook into 65,536 binary16 labels (one per 16-bit state).
+ * kind == KQ_CB_SQG reads `lut` (device, 65,536 E4M3 bytes); other kinds
+ * ignore it.
+ * Replaces the per-state label decoders inlined in the reference kernel:
+ * kquant/csrc/sqg_quantize.cu:17-119 (SQG) and
+ * kquant/csrc/exl3_compat/quant/codebook.cuh:28-124 (MCG, MUL1, 3INST).
+ */
+int kq_build_labels(int kind, const uint8_t* lut, uint16_t* labels, void* stream);
+
+/*
+ * Workspace bytes that kq_viterbi_encode / kq_quantize_tiles_* need for
+ * n_tiles tiles at rate K on the current device.  The figure includes the
+ * 128 KiB label table that kq_quantize_tiles_* build in the workspace.
+ */
+size_t kq_viterbi_workspace_bytes(int K, int64_t n_tiles);
+
+/*
+ * Tail-biting Viterbi encode of n_tiles tiles against prebuilt labels.
+ * out_vals[i] = label(out_states[i]) as float32.  tailbite_ctx in 1..128.
+ * K in {2, 3, 4}.  Bit-exact with the reference kernel
+ * kquant/csrc/qsrt_quantize_tiles_kernel.cuh:21-471 (codes and values).
+ */
+int kq_viterbi_encode(const float* tiles, int64_t n_tiles, int K, const uint16_t* labels,
+                      int tailbite_ctx, float* out_vals, uint16_t* out_states,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Drop-in counterpart of the reference binding quantize_tiles_sqg
+ * (kquant/csrc/sqg_quantize.cpp:23-28, sqg_quantize.cu:165-259).  It differs
+ * in two ways: the LUT is the untransposed state-indexed table, and a single
+ * workspace replaces the temp_costs/temp_edges pair.
+ */
+int kq_quantize_tiles_sqg(const float* tiles, float* out_vals, uint16_t* out_states, int64_t n_tiles,
+                          const uint8_t* lut, int K, int tailbite_ctx,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Drop-in counterpart of quantize_tiles_procedural
+ * (kquant/csrc/sqg_quantize.cpp:29-32, sqg_quantize.cu:261-342).
+ * codebook: KQ_CB_MCG or KQ_CB_MUL1 (KQ_CB_3INST is also accepted).
+ */
+int kq_quantize_tiles_procedural(const float* tiles, float* out_vals, uint16_t* out_states,
+                                 int64_t n_tiles, int K, int codebook, int tailbite_ctx,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Pack the low K bits of every state into 16*K uint16 words per tile in the
+ * native EXL word order: MSB-first 16-symbol groups, then adjacent words
+ * swapped (SWAP16).  Replaces ext.pack_trellis
+ * (kquant/exl3_encoder_backend.py:1666-1677), whose word order
+ * kquant/qsrt.py:811-833 restates.  K in 1..8.
+ */
+int kq_pack_trellis(const uint16_t* states, int64_t n_tiles, int K, uint16_t* packed, void* stream);
+
+/*
+ * Inverse of kq_pack_trellis, plus the cyclic state closure
+ * state_i = ((state_{i-1} << K) | edge_i) & 0xFFFF.  Writes the 16-bit
+ * states.  Replaces kquant/qsrt.py:836-863 (unpack_trellis_edges /
+ * unpack_trellis_states) and kquant/exl3_reference.py:37-61
+ * (reconstruct_trellis_states).  K in 1..8.
+ */
+int kq_unpack_trellis_states(const uint16_t* packed, int64_t n_tiles, int K, uint16_t* states,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KQ_B200_H */

@@ -1,0 +1,179 @@
+"""ctypes binding of ``_kq_b200.so`` (the C ABI in ``include/kq_b200.h``).
+
+Each wrapper takes torch tensors, checks them, and passes raw device pointers
+and torch's current CUDA stream to the library.  There is no CPU fallback:
+without the compiled library or a CUDA device every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "_kq_b200.so"
+
+KQ_CB_3INST = 0
+KQ_CB_MCG = 1
+KQ_CB_MUL1 = 2
+KQ_CB_SQG = 4
+
+EXPORTED = (
+    "kq_last_error",
+    "kq_abi_version",
+    "kq_build_labels",
+    "kq_viterbi_workspace_bytes",
+    "kq_viterbi_encode",
+    "kq_quantize_tiles_sqg",
+    "kq_quantize_tiles_procedural",
+    "kq_pack_trellis",
+    "kq_unpack_trellis_states",
+)
+
+_lib = None
+_lock = threading.Lock()
+
+
+class KQError(RuntimeError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (no device work).  Raises if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise KQError(
+                f"kquant_b200 CUDA library missing at {LIB_PATH}; build it with "
+                "`python -m kquant_b200.build` (there is no CPU fallback)"
+            )
+        L = ctypes.CDLL(str(LIB_PATH))
+        P, I, I64, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+        L.kq_last_error.restype = ctypes.c_char_p
+        L.kq_abi_version.restype = I
+        L.kq_build_labels.argtypes = [I, P, P, P]
+        L.kq_viterbi_workspace_bytes.argtypes = [I, I64]
+        L.kq_viterbi_workspace_bytes.restype = SZ
+        L.kq_viterbi_encode.argtypes = [P, I64, I, P, I, P, P, P, SZ, P]
+        L.kq_quantize_tiles_sqg.argtypes = [P, P, P, I64, P, I, I, P, SZ, P]
+        L.kq_quantize_tiles_procedural.argtypes = [P, P, P, I64, I, I, I, P, SZ, P]
+        L.kq_pack_trellis.argtypes = [P, I64, I, P, P]
+        L.kq_unpack_trellis_states.argtypes = [P, I64, I, P, P]
+        for name in EXPORTED:
+            f = getattr(L, name)
+            if name not in ("kq_last_error", "kq_viterbi_workspace_bytes") and f.restype is ctypes.c_int:
+                f.restype = I
+        _lib = L
+        return L
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().kq_last_error().decode(errors="replace")
+        raise KQError(f"{what} failed with status {rc}: {msg}")
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _cuda(t: torch.Tensor, name: str, dtype: torch.dtype) -> None:
+    if not t.is_cuda:
+        raise KQError(f"{name} must be a CUDA tensor (kquant_b200 has no CPU path)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+# Workspace: one growing uint8 buffer per device, reused across calls on the
+# current stream (calls on one stream are ordered, so reuse is safe).
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[idx] = ws
+    return ws
+
+
+def viterbi_workspace_bytes(K: int, n_tiles: int) -> int:
+    return int(load().kq_viterbi_workspace_bytes(int(K), int(n_tiles)))
+
+
+def build_labels(kind: int, lut: torch.Tensor | None, device: torch.device) -> torch.Tensor:
+    """65,536 binary16 labels (as int16 bits) of a codebook, on ``device``."""
+    out = torch.empty(65536, dtype=torch.int16, device=device)
+    lp = None
+    if kind == KQ_CB_SQG:
+        if lut is None:
+            raise ValueError("SQG labels need a LUT")
+        _cuda(lut, "lut", torch.uint8)
+        if lut.numel() != 65536:
+            raise ValueError("codebook must contain 65,536 uint8 E4M3 values")
+        lp = lut.data_ptr()
+    with torch.cuda.device(device):
+        _check(load().kq_build_labels(int(kind), lp, out.data_ptr(), _stream(device)), "kq_build_labels")
+    return out
+
+
+def viterbi_encode(tiles: torch.Tensor, K: int, labels: torch.Tensor, tailbite_context: int = 128,
+                   out: torch.Tensor | None = None, states: torch.Tensor | None = None):
+    """Encode [N, 256] fp32 tiles; returns (values fp32 [N,256], states int16 [N,256])."""
+    _cuda(tiles, "tiles", torch.float32)
+    _cuda(labels, "labels", torch.int16)
+    if tiles.ndim != 2 or tiles.shape[1] != 256:
+        raise ValueError("tiles must have shape [N, 256]")
+    n = tiles.shape[0]
+    dev = tiles.device
+    if out is None:
+        out = torch.empty_like(tiles)
+    if states is None:
+        states = torch.empty((n, 256), dtype=torch.int16, device=dev)
+    _cuda(out, "out", torch.float32)
+    _cuda(states, "states", torch.int16)
+    if n == 0:
+        return out, states
+    with torch.cuda.device(dev):
+        need = viterbi_workspace_bytes(K, n)
+        if need == 0:
+            raise ValueError(f"unsupported K={K}")
+        ws = workspace(dev, need)
+        _check(load().kq_viterbi_encode(tiles.data_ptr(), n, int(K), labels.data_ptr(), int(tailbite_context),
+                                        out.data_ptr(), states.data_ptr(), ws.data_ptr(), ws.numel(),
+                                        _stream(dev)), "kq_viterbi_encode")
+    return out, states
+
+
+def pack_trellis(states: torch.Tensor, K: int) -> torch.Tensor:
+    """[..., 256] int16 states -> [..., 16K] int16 words (native EXL order)."""
+    _cuda(states, "states", torch.int16)
+    if states.shape[-1] != 256:
+        raise ValueError("states must end in a 256 dimension")
+    n = states.numel() // 256
+    out = torch.empty((*states.shape[:-1], 16 * K), dtype=torch.int16, device=states.device)
+    with torch.cuda.device(states.device):
+        _check(load().kq_pack_trellis(states.data_ptr(), n, int(K), out.data_ptr(), _stream(states.device)),
+               "kq_pack_trellis")
+    return out
+
+
+def unpack_trellis_states(packed: torch.Tensor, K: int) -> torch.Tensor:
+    """[..., 16K] int16 words -> [..., 256] int16 cyclic states."""
+    _cuda(packed, "packed", torch.int16)
+    if packed.shape[-1] != 16 * K:
+        raise ValueError(f"packed tiles must end in {16 * K} int16 words")
+    n = packed.numel() // (16 * K)
+    out = torch.empty((*packed.shape[:-1], 256), dtype=torch.int16, device=packed.device)
+    with torch.cuda.device(packed.device):
+        _check(load().kq_unpack_trellis_states(packed.data_ptr(), n, int(K), out.data_ptr(),
+                                               _stream(packed.device)), "kq_unpack_trellis_states")
+    return out

@@ -1,0 +1,109 @@
+"""GPU parity of the sm_100a Viterbi kernel against the CPU oracle and the reference kernel."""
+import numpy as np
+import pytest
+import torch
+
+from kquant_b200 import codebooks as cb
+
+pytestmark = pytest.mark.gpu
+
+KINDS = {"sqg": 4, "mcg": 1, "mul1": 2, "3inst": 0}
+
+
+def _labels(native, O, kind, K, dev):
+    lut = cb.sqg_xor_cheb_t12_bytes(K) if kind == "sqg" else None
+    lab_dev = native.build_labels(KINDS[kind], lut.to(dev) if lut is not None else None, dev)
+    lab_cpu = O.labels(KINDS[kind], lut.numpy() if lut is not None else None)
+    return lab_dev, lab_cpu
+
+
+def _tiles(kind, n, seed):
+    rng = np.random.default_rng(seed)
+    if kind == "normal":
+        return rng.standard_normal((n, 256)).astype(np.float32)
+    if kind == "zeros":
+        return np.zeros((n, 256), np.float32)
+    if kind == "const":
+        return np.full((n, 256), 0.75, np.float32)
+    if kind == "coarse":      # many exact cost ties
+        return (np.round(rng.standard_normal((n, 256)) * 2) / 2).astype(np.float32)
+    if kind == "wide":
+        return (rng.standard_normal((n, 256)) * 3.0).astype(np.float32)
+    raise ValueError(kind)
+
+
+@pytest.mark.parametrize("K", [2, 3, 4])
+@pytest.mark.parametrize("kind", ["sqg", "mcg", "mul1", "3inst"])
+def test_labels_match_oracle(native, oracle_mod, cuda_device, K, kind):
+    lab_dev, lab_cpu = _labels(native, oracle_mod, kind, K, cuda_device)
+    assert np.array_equal(lab_dev.cpu().numpy().view(np.uint16), lab_cpu)
+
+
+@pytest.mark.parametrize("K", [2, 3, 4])
+@pytest.mark.parametrize("tiles_kind,C", [("normal", 128), ("coarse", 128), ("zeros", 128), ("const", 5),
+                                          ("normal", 1), ("wide", 37), ("coarse", 64)])
+def test_viterbi_matches_oracle(native, oracle_mod, cuda_device, K, tiles_kind, C):
+    O = oracle_mod
+    lab_dev, lab_cpu = _labels(native, O, "sqg", K, cuda_device)
+    tiles = _tiles(tiles_kind, 3, 1000 + K)
+    idx_ref, val_ref, rc = O.viterbi(K, lab_cpu, tiles, C)
+    assert rc == 0
+    vals, states = native.viterbi_encode(torch.from_numpy(tiles).to(cuda_device), K, lab_dev, C)
+    torch.cuda.synchronize()
+    assert np.array_equal(states.cpu().numpy().view(np.uint16), idx_ref)
+    assert np.array_equal(vals.cpu().numpy(), val_ref)
+
+
+@pytest.mark.parametrize("kind", ["mcg", "mul1"])
+@pytest.mark.parametrize("K", [2, 3, 4])
+def test_viterbi_procedural_matches_oracle(native, oracle_mod, cuda_device, K, kind):
+    O = oracle_mod
+    lab_dev, lab_cpu = _labels(native, O, kind, K, cuda_device)
+    tiles = _tiles("normal", 2, 77 + K)
+    idx_ref, val_ref, _ = O.viterbi(K, lab_cpu, tiles, 128)
+    vals, states = native.viterbi_encode(torch.from_numpy(tiles).to(cuda_device), K, lab_dev, 128)
+    assert np.array_equal(states.cpu().numpy().view(np.uint16), idx_ref)
+    assert np.array_equal(vals.cpu().numpy(), val_ref)
+
+
+@pytest.mark.parametrize("K", [2, 3, 4])
+def test_viterbi_multijob_subset_matches_oracle(native, oracle_mod, cuda_device, K):
+    """More tiles than SMs: two staggered tiles per CTA; spot-check against the oracle."""
+    O = oracle_mod
+    lab_dev, lab_cpu = _labels(native, O, "sqg", K, cuda_device)
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    n = 2 * sms + 7
+    tiles = _tiles("coarse", n, 5 + K)
+    vals, states = native.viterbi_encode(torch.from_numpy(tiles).to(cuda_device), K, lab_dev, 128)
+    pick = np.array([0, 1, sms - 1, sms, sms + 1, 2 * sms - 1, 2 * sms, n - 1])
+    idx_ref, val_ref, _ = O.viterbi(K, lab_cpu, tiles[pick], 128)
+    got = states.cpu().numpy().view(np.uint16)[pick]
+    assert np.array_equal(got, idx_ref)
+    assert np.array_equal(vals.cpu().numpy()[pick], val_ref)
+
+
+@pytest.mark.parametrize("K", [2, 3, 4])
+@pytest.mark.parametrize("C", [128, 16])
+def test_viterbi_matches_reference_kernel(native, ref_ext, cuda_device, K, C):
+    """Bit-exact against the reference's own kernel (compiled from its sources) at scale."""
+    lut = cb.sqg_xor_cheb_t12_bytes(K).to(cuda_device)
+    n = 700
+    g = torch.Generator(device=cuda_device).manual_seed(11 + K)
+    tiles = torch.randn((n, 256), generator=g, device=cuda_device)
+    tiles[: n // 2] = torch.round(tiles[: n // 2] * 2) / 2
+    # reference call path: LUT transposed to predecessor-major (kquant/sqg_quantizer.py:130-150)
+    lut_t = lut.reshape(1 << K, (65536 >> K) // 2, 2).permute(1, 0, 2).contiguous().reshape(-1)
+    edges = 65536 >> K
+    dec = edges // (4 if K == 2 else 2)
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    mb = max(256, 3 * sms)
+    costs = torch.zeros((mb, 2, edges), dtype=torch.float16, device=cuda_device)
+    tb = torch.empty((mb, 256, dec), dtype=torch.uint8, device=cuda_device)
+    ref_out = torch.empty_like(tiles)
+    ref_idx = torch.empty((n, 256), dtype=torch.int16, device=cuda_device)
+    ref_ext.quantize_tiles_sqg(tiles, ref_out, ref_idx, costs, tb, lut_t, K, C)
+    lab = native.build_labels(4, lut, cuda_device)
+    vals, states = native.viterbi_encode(tiles, K, lab, C)
+    torch.cuda.synchronize()
+    assert torch.equal(states, ref_idx)
+    assert torch.equal(vals, ref_out)
