@@ -1,0 +1,341 @@
+"""Benchmark: EXL3/QSRT encode of one Kimi-class MoE expert triplet per GPU.
+
+Workload: gate_proj and up_proj (HF [2048, 7168],
+EXL [7168, 2048]) share H13 = X^T X / 8192 from 8192 synthetic tokens of
+hidden 7168; down_proj (HF [7168, 2048], EXL [2048, 7168]) uses H2 from the
+2048 SiLU-gated activations.  Every matrix is encoded at K=3 with the
+production SQG codebook (sqg_xor_cheb_t12), tail-biting context 128.
+
+One step is the complete encode of the triplet through the public plugin API
+(``quantize_uniform_batch``): H finalisation, regularisation, global scale
+search, block-LDLQ with the sm_100a Viterbi kernel, packing and proxy error.
+Under torchrun each rank encodes its own triplet (weak scaling).  NCCL carries
+only the per-step reduce of the proxy statistics.
+
+``value`` times K steps with inputs resident in HBM.  ``e2e`` times the same
+call with the bf16 weights and fp32 Hessians starting in pinned host memory
+and the packed trellis, scales and proxies read back to the host.
+``--impl reference`` times the CPU restatement of the reference tile encoder
+(the reference has no CPU implementation of its own) on a bounded sample of
+the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "EXL3 encoded Mweights/s (K=3, expert triplet)"
+UNIT = "Mweights/s"
+HIDDEN, INTER, TOKENS, K_BITS, CTX = 7168, 2048, 8192, 3, 128
+CONFIG = {"workload": "kimi_expert_triplet_k3", "matrices": "gate,up [7168x2048] + down [2048x7168] (EXL k x n)",
+          "K": K_BITS, "codebook": "sqg_xor_cheb_t12", "tailbite_context": CTX, "tokens": TOKENS,
+          "l2": "inputs larger than L2 (bf16 weights 88 MB + H 222 MB per step)"}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def make_triplet(device: torch.device, seed: int):
+    """Synthetic bf16 expert weights (HF orientation) and the two fp32 Hessians."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def weight(rows, cols):
+        # N(0, 0.015^2) entries, rows scaled by |Student-t(4)| normalised to unit median
+        w = torch.randn((rows, cols), generator=g, device=device) * 0.015
+        z = torch.randn((rows, 5), generator=g, device=device)
+        t = z[:, 0] / torch.sqrt((z[:, 1:] ** 2).sum(1) / 4)
+        s = t.abs() / t.abs().median()
+        return (w * s.unsqueeze(1)).to(torch.bfloat16)
+
+    gate, up, down = weight(INTER, HIDDEN), weight(INTER, HIDDEN), weight(HIDDEN, INTER)
+    chan = torch.exp(torch.randn(HIDDEN, generator=g, device=device))
+    x = torch.randn((TOKENS, HIDDEN), generator=g, device=device) * chan
+    h13 = (x.T @ x) / TOKENS
+    act = torch.nn.functional.silu(x @ gate.float().T) * (x @ up.float().T)
+    h2 = (act.T @ act) / TOKENS
+    del x, act
+    return (gate, up, down), h13.contiguous(), h2.contiguous()
+
+
+def quant_args(matrix: str, device: torch.device, layer: int = 1):
+    from kquant_b200.codebooks import sqg_xor_cheb_t12_bytes
+    idx = ("w1", "w3", "w2").index(matrix)
+    seed = layer * 1_000_000 + idx
+    args = {"K": K_BITS, "seed": seed, "sv_seed": seed + 499_979, "sigma_reg": 0.025, "devices": [str(device)],
+            "device_ratios": None, "apply_out_scales": False, "ldlq_tf32": False, "tailbite_context": CTX,
+            "sqg_e4m3_luts_by_bits": {b: sqg_xor_cheb_t12_bytes(b) for b in (2, 3, 4)}}
+    if matrix in ("w1", "w3"):
+        args["g_scale_into_sv"] = True
+    return args
+
+
+def encode_triplet(weights_exl, h13, h2, device):
+    """One step: encode gate+up (shared H13) and down (H2); returns outputs and proxy stats."""
+    from kquant_b200 import exl3_encoder_backend as be
+    from kquant_b200.ldlq import make_shared_h
+    gate, up, down = weights_exl
+    shared = make_shared_h(HIDDEN, device, h13)
+    r13 = be.quantize_uniform_batch([gate, up], [shared, shared], [quant_args("w1", device), quant_args("w3", device)])
+    r2 = be.quantize_uniform_batch([down], [make_shared_h(INTER, device, h2)], [quant_args("w2", device)])
+    return r13 + r2
+
+
+def to_exl(w_hf: torch.Tensor) -> torch.Tensor:
+    return w_hf.float().T.contiguous()
+
+
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for name, flag in zip(names, parts[5:9]):
+                    if flag.lower() == "active":
+                        reasons.add(name)
+        except OSError:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _reduce_proxy(results, world):
+    """Per-step reduce of the per-tensor proxy statistics (sum, max) across ranks."""
+    vals = torch.tensor([[r[0] for r in results]], dtype=torch.float64, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(vals, op=dist.ReduceOp.SUM)
+    return vals
+
+
+def cpu_tile_rate(seconds_target: float = 15.0):
+    """Oracle (CPU restatement of the reference tile encoder) on all host cores: tiles/s and sample."""
+    import numpy as np
+    from kquant_b200.codebooks import sqg_xor_cheb_t12_bytes
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    lab = O.labels(O.CB_SQG, sqg_xor_cheb_t12_bytes(K_BITS).numpy())
+    rng = np.random.default_rng(0)
+    n = cores
+    t0 = time.perf_counter()
+    O.viterbi(K_BITS, lab, rng.standard_normal((n, 256)).astype(np.float32), CTX, threads=cores)
+    dt = time.perf_counter() - t0
+    reps = max(1, int(seconds_target / max(dt, 1e-3)))
+    n2 = n * reps
+    tiles = rng.standard_normal((n2, 256)).astype(np.float32)
+    t0 = time.perf_counter()
+    O.viterbi(K_BITS, lab, tiles, CTX, threads=cores)
+    dt = time.perf_counter() - t0
+    return n2 / dt, cores, n2
+
+
+def weights_per_step():
+    return 3 * HIDDEN * INTER
+
+
+def run_reference(args, world, rank):
+    """CPU arm: the oracle restatement of the reference tile encoder on the host cores."""
+    if rank != 0:
+        return
+    # tile encodes per step of the GPU arm: every weight tile once, plus the scale search
+    tiles_per_step = weights_per_step() / 256 * 1.22
+    values = []
+    cores = os.cpu_count() or 1
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        rate, cores, n = cpu_tile_rate(seconds_target=6.0 if i < args.warmup else 12.0)
+        if i >= args.warmup:
+            values.append(rate / tiles_per_step * weights_per_step() / 1e6)
+            sample = f"{n} tiles of K={K_BITS} tail-biting Viterbi (C={CTX}) per step, extrapolated to the triplet"
+    v = statistics.median(values)
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": weights_per_step() / (v * 1e6) * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic", "config": CONFIG,
+            "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    args = ap.parse_args()
+    world, rank, local = _dist()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    from kquant_b200 import _native
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _native.load()
+
+    hf, h13, h2 = make_triplet(device, seed=1234 + rank)
+    exl = [to_exl(w) for w in hf]
+
+    def step_resident():
+        return encode_triplet([w.clone() for w in exl], h13, h2, device)
+
+    for _ in range(args.warmup):
+        res = step_resident()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    _native.stats.reset(timing=True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            res = step_resident()
+            proxies = _reduce_proxy(res, world)
+        end.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    elapsed = _allreduce_max(start.elapsed_time(end) / 1e3, world)
+    launches = _native.stats.launches
+    vl, vsec, vtiles, vrelax = _native.stats.viterbi_summary()
+    _native.stats.reset(timing=False)
+    clocks = clk.summary()
+
+    # end-to-end: host (pinned) inputs -> device -> encode -> host outputs
+    host_w = [w.cpu().pin_memory() for w in hf]
+    host_h = [h13.cpu().pin_memory(), h2.cpu().pin_memory()]
+    h2d = sum(t.numel() * t.element_size() for t in host_w + host_h)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    d2h = 0
+    for _ in range(args.e2e_steps):
+        dw = [w.to(device, non_blocking=True) for w in host_w]
+        dh13, dh2 = (h.to(device, non_blocking=True) for h in host_h)
+        out = encode_triplet([to_exl(w) for w in dw], dh13, dh2, device)
+        host_out = [{k: v.cpu() for k, v in o[1].items()} for o in out]
+        proxy_host = _reduce_proxy(out, world).cpu()
+        d2h = sum(v.numel() * v.element_size() for o in host_out for v in o.values()) + proxy_host.numel() * 8
+    ee.record()
+    torch.cuda.synchronize()
+    e_elapsed = _allreduce_max(es.elapsed_time(ee) / 1e3, world)
+
+    total_weights = weights_per_step() * world
+    value = total_weights * args.steps / elapsed / 1e6
+    e2e = total_weights * args.e2e_steps / e_elapsed / 1e6
+    hfma2 = _native.measure_hfma2_rate(device)
+    peak_ops = 2.0 * hfma2 / 1e12                       # fp16 ops/s (two lanes per HFMA2)
+    achieved_ops = 3.0 * vrelax / vsec / 1e12 if vsec > 0 else None
+    traffic = None
+    tpath = ROOT / "profiles" / "viterbi_dram_bytes_per_tile.txt"
+    if tpath.exists() and vl:
+        try:
+            traffic = float(tpath.read_text().split()[0]) * vtiles / vl
+        except (ValueError, IndexError):
+            traffic = None
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 trellis / f32 LDLQ", "data": "synthetic",
+        "config": {**CONFIG, "parallelism": f"expert-sharded x{world}"},
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": {"bound": "alu", "kernel": "kq viterbi_kernel", "achieved": achieved_ops, "peak": peak_ops,
+                     "unit": "Tops/s fp16 (3 ops per relaxation)",
+                     "frac": (achieved_ops / peak_ops) if achieved_ops else None,
+                     "traffic": traffic, "launches": vl, "avg_launch_ms": vsec / vl * 1e3 if vl else None,
+                     "peak_source": "measured HFMA2 rate (kq_probe_hfma2) x 2 lanes, this GPU, this run"},
+        "viterbi_share_of_step": vsec / elapsed if elapsed else None,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, n = cpu_tile_rate()
+        tiles_per_step = vtiles / args.steps
+        cpu_v = rate / tiles_per_step * weights_per_step() / 1e6
+        line["cpu_baseline"] = {"value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": f"{n} tiles of the K={K_BITS} C={CTX} Viterbi on {cores} threads, "
+                                          f"scaled by the GPU step's {tiles_per_step:.0f} tile encodes"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

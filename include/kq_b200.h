@@ -112,6 +112,14 @@ int kq_pack_trellis(const uint16_t* states, int64_t n_tiles, int K, uint16_t* pa
 int kq_unpack_trellis_states(const uint16_t* packed, int64_t n_tiles, int K, uint16_t* states,
                              void* stream);
 
+/*
+ * Roofline probe (no reference counterpart): launches blocks x threads
+ * threads that each issue iters*128 independent __hfma2 instructions.  Time
+ * it with events on `stream`: HFMA2 rate = blocks*threads*iters*128 / time.
+ * The Viterbi kernel's ALU roofline is derived from this measured rate.
+ */
+int kq_probe_hfma2(void* out, int iters, int blocks, int threads, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

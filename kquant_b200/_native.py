@@ -31,6 +31,7 @@ EXPORTED = (
     "kq_quantize_tiles_procedural",
     "kq_pack_trellis",
     "kq_unpack_trellis_states",
+    "kq_probe_hfma2",
 )
 
 _lib = None
@@ -64,6 +65,7 @@ def load() -> ctypes.CDLL:
         L.kq_quantize_tiles_procedural.argtypes = [P, P, P, I64, I, I, I, P, SZ, P]
         L.kq_pack_trellis.argtypes = [P, I64, I, P, P]
         L.kq_unpack_trellis_states.argtypes = [P, I64, I, P, P]
+        L.kq_probe_hfma2.argtypes = [P, I, I, I, P]
         for name in EXPORTED:
             f = getattr(L, name)
             if name not in ("kq_last_error", "kq_viterbi_workspace_bytes") and f.restype is ctypes.c_int:
@@ -89,6 +91,34 @@ def _cuda(t: torch.Tensor, name: str, dtype: torch.dtype) -> None:
         raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
+
+
+# Launch accounting for the benchmark: counts every kernel this library
+# launches and, when enabled, times each Viterbi launch with CUDA events on
+# its stream (algorithmic work = (2C + 256) * 65,536 relaxations per tile).
+class _Stats:
+    def __init__(self):
+        self.launches = 0
+        self.timing = False
+        self.events: list = []
+
+    def reset(self, timing: bool = False):
+        self.launches = 0
+        self.timing = timing
+        self.events = []
+
+    def viterbi_summary(self):
+        """(launches, total seconds, total tiles, total relaxations) of timed Viterbi launches."""
+        total_s, tiles, relax = 0.0, 0, 0
+        for a, b, n, c in self.events:
+            b.synchronize()
+            total_s += a.elapsed_time(b) / 1e3
+            tiles += n
+            relax += n * (2 * c + 256) * 65536
+        return len(self.events), total_s, tiles, relax
+
+
+stats = _Stats()
 
 
 # Workspace: one growing uint8 buffer per device, reused across calls on the
@@ -122,6 +152,7 @@ def build_labels(kind: int, lut: torch.Tensor | None, device: torch.device) -> t
         lp = lut.data_ptr()
     with torch.cuda.device(device):
         _check(load().kq_build_labels(int(kind), lp, out.data_ptr(), _stream(device)), "kq_build_labels")
+    stats.launches += 1
     return out
 
 
@@ -147,9 +178,17 @@ def viterbi_encode(tiles: torch.Tensor, K: int, labels: torch.Tensor, tailbite_c
         if need == 0:
             raise ValueError(f"unsupported K={K}")
         ws = workspace(dev, need)
+        if stats.timing:
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
         _check(load().kq_viterbi_encode(tiles.data_ptr(), n, int(K), labels.data_ptr(), int(tailbite_context),
                                         out.data_ptr(), states.data_ptr(), ws.data_ptr(), ws.numel(),
                                         _stream(dev)), "kq_viterbi_encode")
+        if stats.timing:
+            b.record()
+            stats.events.append((a, b, n, int(tailbite_context)))
+        stats.launches += 1
     return out, states
 
 
@@ -163,6 +202,7 @@ def pack_trellis(states: torch.Tensor, K: int) -> torch.Tensor:
     with torch.cuda.device(states.device):
         _check(load().kq_pack_trellis(states.data_ptr(), n, int(K), out.data_ptr(), _stream(states.device)),
                "kq_pack_trellis")
+    stats.launches += 1
     return out
 
 
@@ -176,4 +216,25 @@ def unpack_trellis_states(packed: torch.Tensor, K: int) -> torch.Tensor:
     with torch.cuda.device(packed.device):
         _check(load().kq_unpack_trellis_states(packed.data_ptr(), n, int(K), out.data_ptr(),
                                                _stream(packed.device)), "kq_unpack_trellis_states")
+    stats.launches += 1
     return out
+
+
+def measure_hfma2_rate(device: torch.device, iters: int = 4096, reps: int = 5) -> float:
+    """Measured HFMA2 instructions per second (lane-level) on ``device``."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    blocks, threads = sms * 4, 512
+    out = torch.zeros(blocks, dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        st = _stream(device)
+        _check(load().kq_probe_hfma2(out.data_ptr(), 64, blocks, threads, st), "kq_probe_hfma2")
+        best = float("inf")
+        for _ in range(reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            _check(load().kq_probe_hfma2(out.data_ptr(), iters, blocks, threads, st), "kq_probe_hfma2")
+            b.record()
+            b.synchronize()
+            best = min(best, a.elapsed_time(b) / 1e3)
+    return blocks * threads * iters * 128 / best

@@ -382,3 +382,1133 @@ def finalize_capture_H(H_data: dict, quant_args: dict, verbose: bool):
         H_data["diag"] = diag
         H_data["q_fallback"] = q_fallback
         return q_fallback, H, L, su, diag
+
+
+# --------------------------------------------------------------------------
+# LDLQ: one backward traversal engine behind every public variant
+# --------------------------------------------------------------------------
+
+
+def mixed_rate_spec(size_k: int, size_n: int, quant_args: dict):
+    """Validate a K2/K3/K4 per-tile rate map (kquant/exl3_encoder_backend.py:508-536)."""
+    rate_axis = quant_args.get("mixed_rate_axis")
+    if rate_axis not in ("k", "n"):
+        raise ValueError("mixed_rate_axis must be 'k' or 'n'")
+    if size_k % 16 or size_n % 16:
+        raise ValueError("mixed-rate LDLQ input must be 16x16 tile aligned")
+    raw = quant_args.get("mixed_tile_bits")
+    if raw is None:
+        raise ValueError("mixed_tile_bits is required for mixed-rate LDLQ")
+    tile_bits = tuple(raw)
+    expected = size_k // 16 if rate_axis == "k" else size_n // 16
+    if len(tile_bits) != expected:
+        raise ValueError(f"mixed_tile_bits has {len(tile_bits)} entries; expected {expected}")
+    if any(isinstance(b, bool) or not isinstance(b, int) or b not in (2, 3, 4) for b in tile_bits):
+        raise ValueError("mixed-rate LDLQ supports only integer K2, K3, and K4")
+    return rate_axis, tile_bits
+
+
+def _baddbmm_ldlq(input, batch1, batch2, *, tf32, inplace=False):
+    """One LDLQ feedback product at the requested FP32 policy (kquant/exl3_encoder_backend.py:725-742)."""
+    previous = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = bool(tf32)
+    try:
+        if inplace:
+            return input.baddbmm_(batch1, batch2)
+        return torch.baddbmm(input, batch1, batch2)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = previous
+
+
+class _RatePlan:
+    """Which K each tile of a 16-row LDLQ step uses, as launch groups.
+
+    ``groups_for(step_tile)`` returns [(K, flat_tile_index or None)], where the
+    flat index enumerates tiles member-major ([B, tiles_n] flattened) and
+    ``None`` means all tiles.
+    """
+
+    def __init__(self, member_bits, rate_axis: str | None, batch: int, tiles_n: int, device):
+        self.rate_axis = rate_axis
+        self.uniform = None
+        self._cache: dict = {}
+        self.device = device
+        self.tiles_n = tiles_n
+        self.batch = batch
+        if rate_axis is None:
+            self.uniform = int(member_bits)
+            return
+        self.member_bits = member_bits
+        if rate_axis == "n":
+            flat = [b for bits in member_bits for b in bits]
+            self._static = self._groups(flat)
+
+    def _groups(self, flat_bits):
+        widths = sorted(set(flat_bits))
+        if len(widths) == 1:
+            return [(widths[0], None)]
+        t = torch.tensor(flat_bits, dtype=torch.int64)
+        return [(w, torch.nonzero(t == w).flatten().to(self.device)) for w in widths]
+
+    def groups_for(self, step_tile: int):
+        if self.uniform is not None:
+            return [(self.uniform, None)]
+        if self.rate_axis == "n":
+            return self._static
+        key = tuple(bits[step_tile] for bits in self.member_bits)
+        g = self._cache.get(key)
+        if g is None:
+            g = self._groups([b for b in key for _ in range(self.tiles_n)])
+            self._cache[key] = g
+        return g
+
+
+def _quantize_step_tiles(tiles: torch.Tensor, plan: _RatePlan, step_tile: int, quant_args: dict):
+    groups = plan.groups_for(step_tile)
+    if len(groups) == 1:
+        args = dict(quant_args)
+        args["K"] = groups[0][0]
+        return quantize_tiles_multigpu(tiles, args)
+    q = torch.empty_like(tiles)
+    idx = torch.empty((tiles.shape[0], 256), dtype=torch.int16, device=tiles.device)
+    for bits, where in groups:
+        args = dict(quant_args)
+        args["K"] = bits
+        gq, gi = quantize_tiles_multigpu(tiles.index_select(0, where), args)
+        q.index_copy_(0, where, gq)
+        idx.index_copy_(0, where, gi)
+    return q, idx
+
+
+def _ldlq_traverse(weights, Ls, quant_args, plan: _RatePlan, *, buffer_rows: int, tf32: bool,
+                   process_begin: int = 0, process_end: int | None = None, state=None,
+                   source_indices: torch.Tensor | None = None, pb=None):
+    """Backward block-LDLQ over rows [process_begin, process_end) of a batch.
+
+    weights [S, k, n] and Ls [S, k, k] are sources; members read source
+    ``source_indices[b]`` (identity when None).  For every 16-row step
+    r0:r1 inside a 128-row buffer [begin, end):
+
+        comp  = P[r0:r1] + L[r1:end, r0:r1]^T (W - What)[r1:end]
+        tiles = tensor-core-ordered 16x16 tiles of W[r0:r1] + comp
+        What[r0:r1], enc[:, r0/16] = Viterbi(tiles)
+
+    and after the buffer P[:begin] += L[begin:end, :begin]^T (W - What)[begin:end]
+    (the dead-prefix trim of kquant/exl3_encoder_backend.py:968-989).
+    Returns (What, enc, P).
+    """
+    S, size_k, size_n = weights.shape
+    B = source_indices.shape[0] if source_indices is not None else S
+    tiles_n = size_n // 16
+    dev = weights.device
+    if process_end is None:
+        process_end = size_k
+    if state is None:
+        wq = weights.new_zeros((B, size_k, size_n))
+        enc = torch.zeros((B, size_k // 16, tiles_n, 256), dtype=torch.int16, device=dev)
+        P = weights.new_zeros((B, size_k, size_n))
+    else:
+        wq, enc, P = state
+    perm = tensor_core_perm(dev)
+    perm_i = tensor_core_perm_i(dev)
+
+    def src(x, sl_rows, sl_cols=None):
+        v = x[:, sl_rows] if sl_cols is None else x[:, sl_rows, sl_cols]
+        return v if source_indices is None else v.index_select(0, source_indices)
+
+    progress = 0
+    for end in range(process_end, process_begin, -buffer_rows):
+        begin = end - buffer_rows
+        for local_end in range(buffer_rows, 0, -16):
+            r0 = begin + local_end - 16
+            r1 = r0 + 16
+            err = src(weights, slice(r1, end)) - wq[:, r1:end]
+            ldl = src(Ls, slice(r1, end), slice(r0, r1))
+            comp = _baddbmm_ldlq(P[:, r0:r1], ldl.transpose(1, 2), err, tf32=tf32)
+            rows = src(weights, slice(r0, r1)) + comp
+            tiles = rows.reshape(B, 16, tiles_n, 16).permute(0, 2, 1, 3).reshape(B * tiles_n, 256)
+            tiles = tiles[:, perm]
+            q, idx = _quantize_step_tiles(tiles, plan, r0 // 16, quant_args)
+            enc[:, r0 // 16] = idx.reshape(B, tiles_n, 256)
+            q = q[:, perm_i]
+            wq[:, r0:r1] = q.reshape(B, tiles_n, 16, 16).permute(0, 2, 1, 3).reshape(B, 16, size_n)
+            if pb:
+                progress += 1
+                pb.update(progress)
+        if begin:
+            err = src(weights, slice(begin, end)) - wq[:, begin:end]
+            ldl = src(Ls, slice(begin, end), slice(0, begin))
+            _baddbmm_ldlq(P[:, :begin], ldl.transpose(1, 2), err, tf32=tf32, inplace=True)
+    return wq, enc, P
+
+
+def _sync(devices):
+    for d in devices:
+        torch.cuda.synchronize(d)
+
+
+def _buffer_rows(quant_args: dict, size_k: int) -> int:
+    rows = max(quant_args.get("buf_size_k", 128), 16)
+    if rows % 16 or size_k % rows:
+        raise ValueError("LDLQ buffer must tile the EXL K dimension")
+    return rows
+
+
+def ldlq(weight: torch.Tensor, L: torch.Tensor, quant_args: dict, pb=None):
+    """Block LDLQ of one matrix at uniform K (kquant/exl3_encoder_backend.py:389-505).
+
+    weight [k, n] fp32, L [k, k] block-LDL factor.  Returns (What [k, n],
+    encoded int16 [k/16, n/16, 256]).
+    """
+    devices = quant_args["devices"]
+    _sync(devices)
+    size_k, size_n = weight.shape
+    assert size_k % 16 == 0 and size_n % 128 == 0
+    assert L.device == torch.device(devices[0])
+    rows = _buffer_rows(quant_args, size_k)
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        w = weight.to(L.device)
+        plan = _RatePlan(int(quant_args["K"]), None, 1, size_n // 16, L.device)
+        wq, enc, _ = _ldlq_traverse(w.unsqueeze(0), L.unsqueeze(0), quant_args, plan, buffer_rows=rows,
+                                    tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
+    _sync(devices)
+    return wq[0].to(weight.device), enc[0].to(weight.device)
+
+
+def ldlq_mixed(weight: torch.Tensor, L: torch.Tensor, quant_args: dict, pb=None):
+    """Dense-H LDLQ with K chosen per tile on one axis (kquant/exl3_encoder_backend.py:539-665)."""
+    devices = quant_args["devices"]
+    _sync(devices)
+    if L.device != torch.device(devices[0]):
+        raise ValueError("mixed-rate LDLQ decomposition is on the wrong device")
+    size_k, size_n = weight.shape
+    axis, bits = mixed_rate_spec(size_k, size_n, quant_args)
+    rows = max(quant_args.get("buf_size_k", 128), 16)
+    if rows % 16 or size_k % rows:
+        raise ValueError("mixed-rate LDLQ buffer must tile the EXL K dimension")
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        w = weight.to(L.device)
+        plan = _RatePlan([bits], axis, 1, size_n // 16, L.device)
+        wq, enc, _ = _ldlq_traverse(w.unsqueeze(0), L.unsqueeze(0), quant_args, plan, buffer_rows=rows,
+                                    tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
+    _sync(devices)
+    return wq[0].to(weight.device), enc[0].to(weight.device)
+
+
+def ldlq_batched(weights: torch.Tensor, Ls: torch.Tensor, quant_args: dict, pb=None):
+    """Same-shape tensors with per-tensor L, one tile launch per step (kquant/exl3_encoder_backend.py:1495-1583)."""
+    devices = quant_args["devices"]
+    _sync(devices)
+    B, size_k, size_n = weights.shape
+    assert weights.device == torch.device(devices[0]) and Ls.device == weights.device
+    assert Ls.shape == (B, size_k, size_k)
+    assert size_k % 16 == 0 and size_n % 128 == 0
+    rows = _buffer_rows(quant_args, size_k)
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        plan = _RatePlan(int(quant_args["K"]), None, B, size_n // 16, weights.device)
+        wq, enc, _ = _ldlq_traverse(weights, Ls, quant_args, plan, buffer_rows=rows,
+                                    tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
+    _sync(devices)
+    return wq, enc
+
+
+def _make_mixed_ldlq_grouping(position_bits, device):
+    """Gather plan (order, inverse, slices) of one step (kquant/exl3_encoder_backend.py:668-698)."""
+    values = tuple(int(v) for v in position_bits)
+    widths = tuple(sorted(set(values)))
+    if len(widths) == 1:
+        return None, None, ((widths[0], 0, len(values)),)
+    order = tuple(p for w in widths for p, v in enumerate(values) if v == w)
+    inverse = [0] * len(order)
+    for grouped, original in enumerate(order):
+        inverse[original] = grouped
+    slices, begin = [], 0
+    for w in widths:
+        end = begin + values.count(w)
+        slices.append((w, begin, end))
+        begin = end
+    return (torch.tensor(order, dtype=torch.int64, device=device),
+            torch.tensor(inverse, dtype=torch.int64, device=device), tuple(slices))
+
+
+def _prepare_mixed_ldlq_groupings(rate_axis, tile_bits, tiles_k, tiles_n, device):
+    """Per-step gather plans for a batch of rate maps (kquant/exl3_encoder_backend.py:701-722)."""
+    if rate_axis == "n":
+        return _make_mixed_ldlq_grouping((v for m in tile_bits for v in m), device), None
+    cache, plans = {}, []
+    for t in range(tiles_k):
+        key = tuple(bits[t] for bits in tile_bits)
+        if key not in cache:
+            cache[key] = _make_mixed_ldlq_grouping((w for w in key for _ in range(tiles_n)), device)
+        plans.append(cache[key])
+    return None, plans
+
+
+def ldlq_mixed_batched(weights, Ls, quant_args_list, pb=None, *, synchronize=True, prepared_groupings=None,
+                       process_begin=0, process_end=None, initial_weights_q=None, initial_encoded_q=None,
+                       initial_product_cache=None, return_product_cache=False, source_indices=None):
+    """Batch independent heterogeneous-rate LDLQ traversals (kquant/exl3_encoder_backend.py:745-996).
+
+    Members may carry different K2/K3/K4 maps on one shared rate axis; a
+    buffer-aligned [process_begin, process_end) interval with continuation
+    state supports exact common-prefix reuse; ``source_indices`` lets members
+    share a source weight/L without copying it.
+    """
+    if weights.ndim != 3 or Ls.ndim != 3:
+        raise ValueError("batched mixed LDLQ expects rank-three weights and Ls")
+    S, size_k, size_n = weights.shape
+    B = len(quant_args_list)
+    if S <= 0 or B <= 0 or Ls.shape != (S, size_k, size_k):
+        raise ValueError("batched mixed LDLQ weight/L shapes do not agree")
+    if weights.dtype != torch.float or Ls.dtype != torch.float:
+        raise TypeError("batched mixed LDLQ weights and Ls must be float32")
+    if weights.device != Ls.device or weights.device.type != "cuda":
+        raise ValueError("batched mixed LDLQ inputs must share one CUDA device")
+    if source_indices is None:
+        if S != B:
+            raise ValueError("batched mixed LDLQ needs one source per member without source_indices")
+    else:
+        if source_indices.shape != (B,) or source_indices.dtype != torch.long or source_indices.device != weights.device:
+            raise ValueError("mixed LDLQ source_indices must be device-local int64 [B]")
+        if bool(torch.any(source_indices < 0)) or bool(torch.any(source_indices >= S)):
+            raise ValueError("mixed LDLQ source_indices are out of range")
+    devices = quant_args_list[0]["devices"]
+    if weights.device != torch.device(devices[0]):
+        raise ValueError("batched mixed LDLQ inputs are on the wrong device")
+    if any(a.get("devices") != devices for a in quant_args_list):
+        raise ValueError("batched mixed LDLQ members must share devices")
+    tf32 = bool(quant_args_list[0].get("ldlq_tf32", False))
+    if any(bool(a.get("ldlq_tf32", False)) != tf32 for a in quant_args_list):
+        raise ValueError("batched mixed LDLQ members must share TF32 policy")
+    if synchronize:
+        _sync(devices)
+    normalized = [mixed_rate_spec(size_k, size_n, a) for a in quant_args_list]
+    axis = normalized[0][0]
+    if any(ax != axis for ax, _ in normalized):
+        raise ValueError("batched mixed LDLQ members must share one rate axis")
+    rows = max(quant_args_list[0].get("buf_size_k", 128), 16)
+    if any(max(a.get("buf_size_k", 128), 16) != rows for a in quant_args_list):
+        raise ValueError("batched mixed LDLQ members must share one buffer size")
+    if rows % 16 or size_k % rows:
+        raise ValueError("batched mixed LDLQ buffer must tile the EXL K dimension")
+    if process_end is None:
+        process_end = size_k
+    if (isinstance(process_begin, bool) or isinstance(process_end, bool)
+            or not isinstance(process_begin, int) or not isinstance(process_end, int)
+            or not 0 <= process_begin < process_end <= size_k
+            or process_begin % rows or process_end % rows):
+        raise ValueError("mixed LDLQ process interval must be buffer-aligned")
+    init = (initial_weights_q, initial_encoded_q, initial_product_cache)
+    if any(v is not None for v in init) and not all(v is not None for v in init):
+        raise ValueError("mixed LDLQ continuation requires all three state tensors")
+    if initial_weights_q is None and process_end != size_k:
+        raise ValueError("a lower mixed LDLQ interval requires continuation state")
+    state = None
+    if initial_weights_q is not None:
+        ew, ee = (B, size_k, size_n), (B, size_k // 16, size_n // 16, 256)
+        if (initial_weights_q.shape != ew or initial_weights_q.dtype != weights.dtype
+                or initial_weights_q.device != weights.device
+                or initial_product_cache.shape != ew or initial_product_cache.dtype != weights.dtype
+                or initial_product_cache.device != weights.device
+                or initial_encoded_q.shape != ee or initial_encoded_q.dtype != torch.int16
+                or initial_encoded_q.device != weights.device):
+            raise ValueError("mixed LDLQ continuation state has invalid shape or type")
+        state = (initial_weights_q, initial_encoded_q, initial_product_cache)
+    del prepared_groupings  # the rate plan below is built once per call and cached per step key
+    plan = _RatePlan([bits for _, bits in normalized], axis, B, size_n // 16, weights.device)
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        wq, enc, P = _ldlq_traverse(weights, Ls, quant_args_list[0], plan, buffer_rows=rows, tf32=tf32,
+                                    process_begin=process_begin, process_end=process_end, state=state,
+                                    source_indices=source_indices, pb=pb)
+    if synchronize:
+        _sync(devices)
+    if return_product_cache:
+        return wq, enc, P
+    return wq, enc
+
+
+def ldlq_mixed_n_candidates_reuse(weights: torch.Tensor, Ls: torch.Tensor, quant_args_groups):
+    """Encode output-axis candidates once per changed tile (kquant/exl3_encoder_backend.py:999-1160).
+
+    LDLQ couples rows, not output columns.  Candidates that differ only in the
+    n-axis rate map share every unchanged output tile.  The all-K3 base is
+    encoded once, the union of each source's K2 / K4 replacement columns once,
+    and the candidates are assembled from those.  Output is source-major.
+    """
+    if weights.ndim != 3 or Ls.ndim != 3:
+        raise ValueError("output-axis reuse expects rank-three weights and Ls")
+    S, size_k, size_n = weights.shape
+    if S <= 0 or Ls.shape != (S, size_k, size_k):
+        raise ValueError("output-axis reuse weight/L shapes do not agree")
+    if len(quant_args_groups) != S or any(not g for g in quant_args_groups):
+        raise ValueError("output-axis reuse needs candidates for every source")
+    maps = []
+    for group in quant_args_groups:
+        norm = [mixed_rate_spec(size_k, size_n, a) for a in group]
+        if any(ax != "n" for ax, _ in norm):
+            raise ValueError("output-axis reuse supports only mixed_rate_axis='n'")
+        if norm[0][1] != (3,) * (size_n // 16):
+            raise ValueError("output-axis reuse requires an all-K3 first candidate")
+        maps.append([bits for _, bits in norm])
+    base_wq, base_enc = ldlq_mixed_batched(weights, Ls, [g[0] for g in quant_args_groups])
+
+    specs = []
+    for s, cand in enumerate(maps):
+        width = {}
+        for bits in cand[1:]:
+            for tile, w in enumerate(bits):
+                if w == 3:
+                    continue
+                if width.setdefault(tile, w) != w:
+                    raise ValueError("one output tile uses multiple non-K3 widths across candidates")
+        for w in (2, 4):
+            pos = tuple(t for t, x in width.items() if x == w)
+            if pos:
+                specs.append((s, w, pos))
+    dev = weights.device
+
+    def cols(tiles):
+        return torch.tensor([c for t in tiles for c in range(16 * t, 16 * t + 16)], dtype=torch.int64, device=dev)
+
+    overrides = {}
+    for count in sorted({len(p) for _, _, p in specs}):
+        members = [sp for sp in specs if len(sp[2]) == count]
+        mw = torch.stack([weights[s].index_select(1, cols(pos)) for s, _, pos in members])
+        mL = torch.stack([Ls[s] for s, _, _ in members])
+        margs = []
+        for s, w, _ in members:
+            a = dict(quant_args_groups[s][0])
+            a["mixed_tile_bits"] = (w,) * count
+            margs.append(a)
+        owq, oenc = ldlq_mixed_batched(mw, mL, margs)
+        for i, (s, w, pos) in enumerate(members):
+            overrides[(s, w)] = (pos, owq[i], oenc[i])
+
+    out_wq, out_enc = [], []
+    for s, cand in enumerate(maps):
+        for c, bits in enumerate(cand):
+            if c == 0:
+                out_wq.append(base_wq[s])
+                out_enc.append(base_enc[s])
+                continue
+            wq = base_wq[s].clone()
+            enc = base_enc[s].clone()
+            for w in (2, 4):
+                target = tuple(t for t, x in enumerate(bits) if x == w)
+                if not target:
+                    continue
+                pos, rwq, renc = overrides[(s, w)]
+                local = {t: i for i, t in enumerate(pos)}
+                lt = tuple(local[t] for t in target)
+                wq.index_copy_(1, cols(target), rwq.index_select(1, cols(lt)))
+                enc.index_copy_(1, torch.tensor(target, dtype=torch.int64, device=dev),
+                                renc.index_select(1, torch.tensor(lt, dtype=torch.int64, device=dev)))
+            out_wq.append(wq)
+            out_enc.append(enc)
+    return torch.stack(out_wq), torch.stack(out_enc)
+
+
+def ldlq_mixed_k_candidates_prefix_reuse(weights: torch.Tensor, Ls: torch.Tensor, quant_args_groups):
+    """Input-axis candidates through a shared backward prefix (kquant/exl3_encoder_backend.py:1163-1345).
+
+    The common buffer-aligned suffix of each source's rate maps is traversed
+    once; the remaining rows proceed as a trie of live LDLQ states, forking
+    only where candidate maps diverge.  Results equal independent traversals.
+    """
+    if weights.ndim != 3 or Ls.ndim != 3:
+        raise ValueError("input-axis prefix reuse expects rank-three weights and Ls")
+    S, size_k, size_n = weights.shape
+    if S <= 0 or Ls.shape != (S, size_k, size_k):
+        raise ValueError("input-axis prefix reuse weight/L shapes do not agree")
+    if len(quant_args_groups) != S or any(not g for g in quant_args_groups):
+        raise ValueError("input-axis prefix reuse needs candidates for every source")
+    if not any(len(g) > 1 for g in quant_args_groups):
+        raise ValueError("input-axis prefix reuse needs at least one multi-candidate source")
+    maps, starts = [], []
+    for group in quant_args_groups:
+        norm = [mixed_rate_spec(size_k, size_n, a) for a in group]
+        if any(ax != "k" for ax, _ in norm):
+            raise ValueError("input-axis prefix reuse supports only mixed_rate_axis='k'")
+        m = [bits for _, bits in norm]
+        start = len(m[0])
+        while start > 0 and len({bits[start - 1] for bits in m}) == 1:
+            start -= 1
+        maps.append(m)
+        starts.append(start)
+    rows = max(quant_args_groups[0][0].get("buf_size_k", 128), 16)
+    if any(max(a.get("buf_size_k", 128), 16) != rows for g in quant_args_groups for a in g):
+        raise ValueError("input-axis prefix reuse requires one LDLQ buffer size")
+    split = -(-max(starts) * 16 // rows) * rows
+    flat = [(s, c) for s, g in enumerate(quant_args_groups) for c in range(len(g))]
+    dev = weights.device
+    if split >= size_k:
+        return ldlq_mixed_batched(torch.stack([weights[s] for s, _ in flat]), torch.stack([Ls[s] for s, _ in flat]),
+                                  [quant_args_groups[s][c] for s, c in flat])
+    wq, enc, P = ldlq_mixed_batched(weights, Ls, [g[0] for g in quant_args_groups], process_begin=split,
+                                    process_end=size_k, return_product_cache=True)
+    if split == 0:
+        src = torch.tensor([s for s, _ in flat], dtype=torch.long, device=dev)
+        return wq.index_select(0, src), enc.index_select(0, src)
+    nodes = [(s, tuple(range(len(g)))) for s, g in enumerate(quant_args_groups)]
+    devices = quant_args_groups[0][0]["devices"]
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        for end in range(split, 0, -rows):
+            begin = end - rows
+            t0, t1 = begin // 16, end // 16
+            children, parents, args = [], [], []
+            for parent, (s, cands) in enumerate(nodes):
+                parts: dict = {}
+                for c in cands:
+                    parts.setdefault(maps[s][c][t0:t1], []).append(c)
+                for members in parts.values():
+                    children.append((s, tuple(members)))
+                    parents.append(parent)
+                    args.append(quant_args_groups[s][members[0]])
+            if len(children) != len(nodes) or any(p != i for i, p in enumerate(parents)):
+                pidx = torch.tensor(parents, dtype=torch.long, device=dev)
+                wq, enc, P = wq.index_select(0, pidx), enc.index_select(0, pidx), P.index_select(0, pidx)
+            nodes = children
+            srcs = torch.tensor([s for s, _ in nodes], dtype=torch.long, device=dev)
+            wq, enc, P = ldlq_mixed_batched(weights, Ls, args, synchronize=False, process_begin=begin,
+                                            process_end=end, initial_weights_q=wq, initial_encoded_q=enc,
+                                            initial_product_cache=P, return_product_cache=True,
+                                            source_indices=srcs)
+    _sync(devices)
+    where = {}
+    for i, (s, cands) in enumerate(nodes):
+        for c in cands:
+            where[(s, c)] = i
+    if set(where) != set(flat):
+        raise AssertionError("input-axis prefix trie lost a rate candidate")
+    out = torch.tensor([where[m] for m in flat], dtype=torch.long, device=dev)
+    return wq.index_select(0, out), enc.index_select(0, out)
+
+
+def fallback_quant(weight: torch.Tensor, q_device, quant_args: dict, pb=None):
+    """Tile quantization without feedback, for an unusable H (kquant/exl3_encoder_backend.py:1348-1463).
+
+    Returns (What, encoded, mse).
+    """
+    devices = quant_args["devices"]
+    _sync(devices)
+    size_k, size_n = weight.shape
+    assert size_k % 16 == 0 and size_n % 128 == 0
+    assert weight.device == torch.device(devices[0])
+    tn = size_n // 16
+    dev = weight.device
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        tiles = weight.reshape(size_k // 16, 16, tn, 16).permute(0, 2, 1, 3).reshape(-1, 256)
+        tiles = tiles[:, tensor_core_perm(dev)]
+        q, idx = quantize_tiles_multigpu(tiles, quant_args)
+        q = q[:, tensor_core_perm_i(dev)]
+        wq = q.reshape(size_k // 16, tn, 16, 16).permute(0, 2, 1, 3).reshape(size_k, size_n)
+        enc = idx.reshape(size_k // 16, tn, 256)
+        mse = (torch.sum((weight.float() - wq.float()).pow(2), dtype=torch.float64) / weight.numel()).item()
+        if pb:
+            pb.update(size_k // 16)
+    _sync(devices)
+    return wq, enc, mse
+
+
+# --------------------------------------------------------------------------
+# proxy error, packing
+# --------------------------------------------------------------------------
+
+
+def block_trace_parts(A, B, block_size=1024):
+    """Column-block terms of trace(A^T B A), on device (kquant/exl3_encoder_backend.py:1466-1479)."""
+    parts = []
+    for j in range(0, B.shape[1], block_size):
+        k = min(j + block_size, B.shape[1])
+        parts.append(torch.sum((A.T @ B[:, j:k]) * A[j:k, :].T))
+    return torch.stack(parts)
+
+
+def block_trace(A, B, block_size=1024):
+    """trace(A^T B A) summed in fp64 on the host (kquant/exl3_encoder_backend.py:1482-1492)."""
+    total = 0.0
+    for p in block_trace_parts(A, B, block_size).cpu():
+        total += p.item()
+    return total
+
+
+def pack_trellis(encoded: torch.Tensor, quant_args: dict) -> torch.Tensor:
+    """[tk, tn, 256] int16 states -> [tk, tn, 16K] int16 words (kquant/exl3_encoder_backend.py:1666-1677)."""
+    K = quant_args["K"]
+    assert encoded.ndim == 3 and encoded.shape[2] == 256
+    assert encoded.dtype == torch.int16
+    return _native.pack_trellis(encoded.contiguous(), int(K))
+
+
+# --------------------------------------------------------------------------
+# global scale search (kquant/exl3_encoder_backend.py:1688-1808)
+# --------------------------------------------------------------------------
+
+
+def sample_scale_tiles(weight_r: torch.Tensor, width: int = 3) -> torch.Tensor:
+    """Wrapped-diagonal tiles plus the highest- and lowest-RMS tiles, tensor-core ordered."""
+    dev = weight_r.device
+    tk, tn = weight_r.shape[0] // 16, weight_r.shape[1] // 16
+    w4 = weight_r.view(tk, 16, tn, 16)
+    diag = max(tk, tn)
+    ii = torch.arange(diag, device=dev).repeat_interleave(width)
+    ww = torch.arange(width, device=dev).repeat(diag)
+    kk, nn = ii % tk, (ii + ww) % tn
+    num_x = max(8, (diag * width) // 16)
+    ms = w4.square().mean(dim=(1, 3)).flatten()
+    num_x = min(num_x, (ms.shape[0] + 1) // 2)
+    ext = torch.cat((torch.topk(ms, num_x).indices, torch.topk(ms, num_x, largest=False).indices))
+    tiles = w4[torch.cat((kk, ext // tn)), :, torch.cat((nn, ext % tn)), :].reshape(-1, 256)
+    return tiles[:, tensor_core_perm(dev)].contiguous()
+
+
+def g_scale_search_batch(samples: list[torch.Tensor], quant_args: dict):
+    """Coarse grid (0.1..1.9 on a 1/3 subsample), fine 5-point grid, parabolic refine.
+
+    Returns [(scale, mse tensor)] per sample set; all evaluations of a stage
+    share as few tile launches as the 65,536-tile batch limit allows.
+    """
+    n_t = len(samples)
+    dev = samples[0].device
+    max_tiles = 65536
+
+    def evaluate(pairs, sets):
+        out = torch.empty(len(pairs), dtype=torch.float, device=dev)
+        i = 0
+        while i < len(pairs):
+            j, tot = i, 0
+            while j < len(pairs) and tot + sets[pairs[j][0]].shape[0] <= max_tiles:
+                tot += sets[pairs[j][0]].shape[0]
+                j += 1
+            j = max(j, i + 1)
+            batch = torch.cat([sets[t] * s for t, s in pairs[i:j]])
+            q, _ = quantize_tiles_multigpu(batch, quant_args)
+            off = 0
+            for p, (t, s) in enumerate(pairs[i:j]):
+                cnt = sets[t].shape[0]
+                out[i + p] = (q[off:off + cnt] / s - sets[t]).square().mean()
+                off += cnt
+            i = j
+        return out
+
+    coarse = [0.1 + 0.2 * i for i in range(10)]
+    subs = [s[::3] for s in samples]
+    mse1 = evaluate([(t, s) for t in range(n_t) for s in coarse], subs).view(n_t, len(coarse))
+    centers = [coarse[c] for c in mse1.argmin(dim=1).tolist()]
+    step = 0.075
+    fine = [[c + step * (i - 2) for i in range(5)] for c in centers]
+    mse2 = evaluate([(t, s) for t in range(n_t) for s in fine[t]], samples).view(n_t, 5)
+    host = mse2.tolist()
+    results = []
+    for t in range(n_t):
+        best = min(range(5), key=lambda i: host[t][i])
+        offset = 0.0
+        if 0 < best < 4:
+            y0, y1, y2 = host[t][best - 1], host[t][best], host[t][best + 1]
+            denom = y0 - 2.0 * y1 + y2
+            offset = 0.5 * (y0 - y2) / denom if denom > 0 else 0.0
+            offset = max(-0.5, min(0.5, offset))
+        results.append((max(fine[t][best] + offset * step, 0.01), mse2[t, best]))
+    return results
+
+
+def g_scale_gss(weight_r: torch.Tensor, verbose: bool, quant_args: dict, width: int = 3, pb=None):
+    devices = quant_args["devices"]
+    _sync(devices)
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        tiles = sample_scale_tiles(weight_r, width)
+        if pb:
+            pb.update(50)
+        best_scale, best_mse = g_scale_search_batch([tiles], quant_args)[0]
+        if pb:
+            pb.update(100)
+        if verbose:
+            print(f"     - scale search: min = {best_scale:.6f}, mse: {best_mse.item():.6f}")
+    _sync(devices)
+    return best_scale, best_mse
+
+
+# --------------------------------------------------------------------------
+# regularisation (kquant/exl3_encoder_backend.py:1811-2042)
+# --------------------------------------------------------------------------
+
+
+def block_rms(x: torch.Tensor, dim: int, keepdim: bool = False, blocksize: int = 32):
+    """sqrt(mean(x^2, dim)) accumulated over blocks of ``blocksize`` along ``dim``."""
+    acc = None
+    for blk in torch.split(x, blocksize, dim=dim):
+        part = blk.square().sum(dim=dim, keepdim=keepdim)
+        acc = part if acc is None else acc + part
+    return (acc / x.size(dim)).sqrt()
+
+
+def block_rms_n(x: torch.Tensor, dim: int = 0, blocksize: int = 32):
+    acc, n = None, 0
+    for blk in torch.split(x, blocksize, dim=dim):
+        part = blk.square().sum()
+        n += blk.numel()
+        acc = part if acc is None else acc + part
+    return (acc / n).sqrt()
+
+
+def block_nmse(x: torch.Tensor, y: torch.Tensor, dim: int = 0, blocksize: int = 32):
+    sq = diff = None
+    for bx, by in zip(torch.split(x, blocksize, dim=dim), torch.split(y, blocksize, dim=dim)):
+        a, b = by.square().sum(), (bx - by).square().sum()
+        sq = a if sq is None else sq + a
+        diff = b if diff is None else diff + b
+    return diff.item() / (sq.item() + 1e-20)
+
+
+_SHARED_INPUT_SCALES: dict = {}
+
+
+def output_signs(n: int, device, quant_args: dict) -> torch.Tensor:
+    """Output sign flips, optionally from their own seed (kquant/exl3_encoder_backend.py:1867-1877)."""
+    if "sv_seed" in quant_args:
+        torch.manual_seed(quant_args["sv_seed"])
+    return (torch.randn(n, device=device).sign() + 1e-5).sign().to(torch.float).unsqueeze(0)
+
+
+def relocate_g_scale_to_sv(su: torch.Tensor, sv: torch.Tensor, g_scale: float):
+    if not math.isfinite(float(g_scale)) or float(g_scale) <= 0.0:
+        raise ValueError("g_scale must be positive and finite")
+    return su * g_scale, sv / g_scale
+
+
+def apply_g_scale(weight, su, sv, g_scale: float, *, into_sv: bool = False):
+    """Scale the regularised weight; fold 1/g into ``sv`` or ``su`` (kquant/exl3_encoder_backend.py:2018-2042)."""
+    if not math.isfinite(float(g_scale)) or float(g_scale) <= 0.0:
+        raise ValueError("g_scale must be positive and finite")
+    weight *= g_scale
+    if into_sv:
+        sv /= g_scale
+    else:
+        su /= g_scale
+    return weight, su, sv
+
+
+def regularize(weight, su, sv, quant_args: dict, verbose: bool, H_diag, pb, skip_g_scale: bool = False,
+               q_fallback: bool = False):
+    """Sign flips, channel RMS scales and both block Hadamards, then the global scale.
+
+    ``weight`` is transformed in place.  Returns (apply_out_scales, weight,
+    g_scale, su, sv) (kquant/exl3_encoder_backend.py:1880-1999).
+    """
+    force = quant_args["apply_out_scales"]
+    if not q_fallback and H_diag is not None:
+        d = torch.sort(H_diag.sqrt(), descending=True).values
+        skew = d[: d.shape[0] // 50].sum() / d.sum()
+        if verbose:
+            print(f"     - input state skew: {skew.item():.6f}")
+        apply_out = (skew.item() < 0.15) if force is None else force
+    else:
+        apply_out = True if force is None else force
+    if q_fallback:
+        apply_out = force
+    ocs = block_rms(weight, dim=0, keepdim=True)
+    mean = ocs.mean().item()
+    if mean > 1e-30:
+        ocs /= mean
+        quant_args["zeros"] = False
+    else:
+        quant_args["zeros"] = True
+        if force is not None:
+            apply_out = True
+    zero_cols = ocs.abs() < 1e-30
+    if apply_out:
+        ocs[zero_cols] = 0.1
+        sv = (sv * ocs + 1e-10).float()
+    weight /= sv
+    sv[zero_cols] = 0.0
+    blockwise_preapply_had_r_(weight, had_n)
+    ics = block_rms(weight, dim=1, keepdim=True)
+    ics[ics.abs() < 1e-30] = 0.1
+    key = quant_args.get("shared_input_scales_key")
+    if key is not None:
+        ics = _SHARED_INPUT_SCALES.setdefault(key, ics)
+    su = (su * ics / (-codebook_scale) + 1e-10).float()
+    weight /= su
+    blockwise_preapply_had_l_(weight, had_k)
+    mse_scale = None
+    if not skip_g_scale:
+        g_scale, mse_scale = g_scale_gss(weight, False, quant_args, pb=pb)
+    else:
+        g_scale = 1.0
+    weight, su, sv = apply_g_scale(weight, su, sv, g_scale, into_sv=bool(quant_args.get("g_scale_into_sv")))
+    if verbose:
+        print(f"     - su/sv std: {su.std().item():.6f}   {sv.std().item():.6f}")
+        print(f"     - global scale: {g_scale:.6f}")
+        if mse_scale is not None:
+            print(f"     - sample mse: {mse_scale.item():.6f}")
+        print(f"     - apply_out_scales: {apply_out}")
+    return apply_out, weight, g_scale, su, sv
+
+
+# --------------------------------------------------------------------------
+# top-level encoders (kquant/exl3_encoder_backend.py:2045-2765)
+# --------------------------------------------------------------------------
+
+
+class _NoProgress:
+    def __init__(self, *args, **kwargs):
+        pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return None
+
+    def update(self, value):
+        return None
+
+    def new_task(self, text, count):
+        return None
+
+
+ProgressBar = _NoProgress
+
+
+def _codebook_tensors(quant_args: dict) -> dict:
+    out = {}
+    if quant_args.get("mcg"):
+        out["mcg"] = torch.tensor(codebook_mcg_mult, dtype=torch.uint32).view(torch.int)
+    if quant_args.get("mul1"):
+        out["mul1"] = torch.tensor(codebook_mul1_mult, dtype=torch.uint32).view(torch.int)
+    return out
+
+
+def _reconstruct(wq: torch.Tensor, su: torch.Tensor, sv: torch.Tensor) -> torch.Tensor:
+    """Original-basis weight: had_r(had_l(What) * su) * sv."""
+    w = preapply_had_l(wq, had_k)
+    w *= su
+    w = preapply_had_r(w, had_n)
+    w *= sv
+    return w
+
+
+def quantize_qsrt(weight: torch.Tensor, H_data: dict, quant_args: dict, return_weight_q: bool,
+                  progress_str: str | None = None, verbose: bool = False,
+                  swap_to_device: torch.device | None = None, save_reg: str | None = None):
+    """Encode one [k, n] fp32 matrix against its captured Hessian.
+
+    Returns (weight_q or None, proxy error, {"suh", "svh", "trellis"} plus
+    "mcg"/"mul1" markers) and updates ``quant_args`` with
+    apply_out_scales / g_scale / q_fallback (kquant/exl3_encoder_backend.py:2045-2255).
+    """
+    assert weight.dtype == torch.float
+    if "seed" in quant_args:
+        torch.manual_seed(quant_args["seed"])
+    devices = quant_args["devices"]
+    if weight.device != torch.device(devices[0]):
+        weight = weight.to(devices[0])
+    device = weight.device if swap_to_device is None else swap_to_device
+    k, n = weight.shape
+    tiles_k = k // 16
+    q_fallback, H, L, su, H_diag = finalize_capture_H(H_data, quant_args, verbose)
+    if H is not None and H.is_cuda:
+        H = H.to(device)
+    if su.is_cuda:
+        su = su.to(device)
+    if H_diag is not None and H_diag.is_cuda:
+        H_diag = H_diag.to(device)
+    sv = output_signs(n, device, quant_args)
+    if H_data["L"] is not None:
+        H_data["L"] = H_data["L"].cpu()
+    if L is not None:
+        L = L.to(device)
+    if swap_to_device is not None:
+        weight = weight.to(swap_to_device)
+    weight_ref = weight.cpu() if verbose else None
+    apply_out_scales, weight_r, g_scale, su, sv = regularize(weight, su, sv, quant_args, verbose, H_diag, None,
+                                                             q_fallback=q_fallback)
+    del weight
+    mixed = "mixed_rate_axis" in quant_args or "mixed_tile_bits" in quant_args
+    if not q_fallback:
+        if mixed:
+            weight_q, encoded_q = ldlq_mixed(weight_r, L, quant_args)
+        else:
+            weight_q, encoded_q = ldlq(weight_r, L, quant_args)
+        del L
+        try:
+            Hd = H.to(device)
+            num = block_trace(weight_r - weight_q, Hd)
+            den = block_trace(weight_r, Hd)
+            proxy_err = num / max(den, 1e-8)
+        except torch.OutOfMemoryError:
+            proxy_err = -1.0
+    else:
+        if mixed:
+            raise ValueError("mixed-rate quantization requires a non-fallback dense Hessian")
+        weight_q, encoded_q, proxy_err = fallback_quant(weight_r, device, quant_args)
+    if return_weight_q or verbose:
+        weight_q = _reconstruct(weight_q.to(device), su, sv)
+        if verbose:
+            print(f"     - quant nmse: {block_nmse(weight_q, weight_ref.to(device)):.6f}")
+    suh = su.flatten().contiguous().to(dtype=torch.half, copy=True)
+    svh = sv.flatten().contiguous().to(dtype=torch.half, copy=True)
+    pack_fn = quant_args.get("pack_trellis_fn", pack_trellis)
+    trellis = pack_fn(encoded_q.to(device), quant_args)
+    out_tensors = {"suh": suh, "svh": svh, "trellis": trellis, **_codebook_tensors(quant_args)}
+    quant_args.update({"apply_out_scales": apply_out_scales, "g_scale": g_scale, "q_fallback": q_fallback})
+    return weight_q, proxy_err, out_tensors
+
+
+_PREP_KEYS = ("K", "seed", "sv_seed", "sigma_reg", "devices", "device_ratios", "apply_out_scales", "mcg", "mul1",
+              "shared_input_scales_key", "g_scale_into_sv", "buf_size_k", "ldlq_tf32", "tailbite_context",
+              "g_scale_override")
+
+
+def _trace_rows(parts: list[torch.Tensor]) -> list[float]:
+    """Sum each row of block-trace terms on the host, in order, in fp64."""
+    if not parts:
+        return []
+    rows = torch.stack(parts).cpu()
+    values = []
+    for row in rows:
+        total = 0.0
+        for p in row:
+            total += p.item()
+        values.append(total)
+    return values
+
+
+def quantize_qsrt_batch(weights: list[torch.Tensor], H_datas: list[dict], quant_args_groups: list[list[dict]], *,
+                        return_weight_q: bool = True, verbose: bool = False):
+    """Prepare each source once and encode all of its rate candidates together.
+
+    Returns, per source, a list of {"weight_q", "encoded", "suh", "svh",
+    "proxy", "g_scale"} (kquant/exl3_encoder_backend.py:2258-2535).
+    """
+    S = len(weights)
+    if S <= 0 or len(H_datas) != S or len(quant_args_groups) != S:
+        raise ValueError("QSRT batch inputs must have equal nonzero lengths")
+    if any(not g for g in quant_args_groups):
+        raise ValueError("every QSRT source needs at least one rate candidate")
+    if any(w.ndim != 2 or w.dtype != torch.float for w in weights):
+        raise TypeError("QSRT batch weights must be float32 matrices")
+    shape = weights[0].shape
+    if any(w.shape != shape for w in weights):
+        raise ValueError("QSRT batch sources must have one matrix shape")
+    for group in quant_args_groups:
+        ref = group[0]
+        for args in group:
+            mixed_rate_spec(shape[0], shape[1], args)
+            for key in _PREP_KEYS:
+                if args.get(key) != ref.get(key):
+                    raise ValueError(f"QSRT candidates changed preparation argument {key}")
+    devices = quant_args_groups[0][0]["devices"]
+    device = torch.device(devices[0])
+    if any(g[0].get("devices") != devices for g in quant_args_groups):
+        raise ValueError("QSRT source groups must share devices")
+    if any(w.device != device for w in weights):
+        raise ValueError("QSRT batch weights must already be on the quant device")
+
+    prepared = []
+    for weight, H_data, group in zip(weights, H_datas, quant_args_groups):
+        args = group[0]
+        if "seed" in args:
+            torch.manual_seed(args["seed"])
+        q_fallback, H, L, su, H_diag = finalize_capture_H(H_data, args, verbose)
+        if q_fallback or H is None or L is None:
+            raise ValueError("mixed-rate batching requires a non-fallback dense Hessian")
+        H, L, su = H.to(device), L.to(device), su.to(device)
+        if H_diag is not None:
+            H_diag = H_diag.to(device)
+        if H_data["L"] is not None:
+            H_data["L"] = H_data["L"].cpu()
+        sv = output_signs(weight.shape[1], device, args)
+        apply_out, weight_r, _, su, sv = regularize(weight, su, sv, args, verbose, H_diag, None, skip_g_scale=True)
+        prepared.append({"H": H, "L": L, "weight_r": weight_r, "su": su, "sv": sv, "apply_out_scales": apply_out})
+
+    scales: list = [None] * S
+    search_sources, search_samples = [], []
+    for s, (item, group) in enumerate(zip(prepared, quant_args_groups)):
+        override = group[0].get("g_scale_override")
+        if override is None:
+            search_sources.append(s)
+            search_samples.append(sample_scale_tiles(item["weight_r"]))
+        else:
+            if (isinstance(override, bool) or not isinstance(override, (int, float))
+                    or not math.isfinite(float(override)) or float(override) <= 0.0):
+                raise ValueError("g_scale_override must be positive and finite")
+            scales[s] = (float(override), None)
+    if search_samples:
+        for s, res in zip(search_sources, g_scale_search_batch(search_samples,
+                                                               quant_args_groups[search_sources[0]][0])):
+            scales[s] = res
+    del search_samples
+    if any(r is None for r in scales):
+        raise AssertionError("global scale search did not cover every source")
+    for item, group, (g_scale, _) in zip(prepared, quant_args_groups, scales):
+        item["weight_r"], item["su"], item["sv"] = apply_g_scale(
+            item["weight_r"], item["su"], item["sv"], g_scale, into_sv=bool(group[0].get("g_scale_into_sv")))
+        item["g_scale"] = g_scale
+
+    flat = [(s, c) for s, g in enumerate(quant_args_groups) for c in range(len(g))]
+    specs = [[mixed_rate_spec(shape[0], shape[1], a) for a in g] for g in quant_args_groups]
+    reuse_n = all(all(ax == "n" for ax, _ in sp) and sp[0][1] == (3,) * (shape[1] // 16) for sp in specs)
+    reuse_k = any(len(g) > 1 for g in quant_args_groups) and all(all(ax == "k" for ax, _ in sp) for sp in specs)
+    source_weights = None
+    if reuse_n:
+        source_weights = torch.stack([it["weight_r"] for it in prepared])
+        weights_q, encoded_q = ldlq_mixed_n_candidates_reuse(
+            source_weights, torch.stack([it["L"] for it in prepared]), quant_args_groups)
+    elif reuse_k:
+        source_weights = torch.stack([it["weight_r"] for it in prepared])
+        weights_q, encoded_q = ldlq_mixed_k_candidates_prefix_reuse(
+            source_weights, torch.stack([it["L"] for it in prepared]), quant_args_groups)
+    else:
+        weights_batch = torch.stack([prepared[s]["weight_r"] for s, _ in flat])
+        weights_q, encoded_q = ldlq_mixed_batched(
+            weights_batch, torch.stack([prepared[s]["L"] for s, _ in flat]),
+            [quant_args_groups[s][c] for s, c in flat])
+
+    den_parts = [block_trace_parts(it["weight_r"], it["H"]) for it in prepared]
+    num_parts, pending = [], []
+    for f, (s, c) in enumerate(flat):
+        item = prepared[s]
+        args = quant_args_groups[s][c]
+        src = source_weights[s] if source_weights is not None else weights_batch[f]
+        num_parts.append(block_trace_parts(src - weights_q[f], item["H"]))
+        if "suh" not in item:
+            item["suh"] = item["su"].flatten().contiguous().to(dtype=torch.half, copy=True)
+            item["svh"] = item["sv"].flatten().contiguous().to(dtype=torch.half, copy=True)
+        recon = None
+        if return_weight_q:
+            recon = _reconstruct(weights_q[f], item["suh"].float().unsqueeze(1),
+                                 item["svh"].float().unsqueeze(0)).contiguous()
+        args.update({"apply_out_scales": item["apply_out_scales"], "g_scale": item["g_scale"], "q_fallback": False,
+                     "zeros": quant_args_groups[s][0].get("zeros", False)})
+        pending.append((s, recon, encoded_q[f].contiguous(), item["suh"], item["svh"]))
+    traces = _trace_rows(den_parts + num_parts)
+    dens, nums = traces[:S], traces[S:]
+    results = [[] for _ in range(S)]
+    for num, (s, recon, enc, suh, svh) in zip(nums, pending):
+        results[s].append({"weight_q": recon, "encoded": enc, "suh": suh, "svh": svh,
+                           "proxy": num / max(dens[s], 1e-8), "g_scale": prepared[s]["g_scale"]})
+    return results
+
+
+def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], quant_args_list: list[dict],
+                           progress_str: str | None = None, verbose: bool = False):
+    """Encode same-K linears together (kquant/exl3_encoder_backend.py:2538-2765).
+
+    A shared H object concatenates the regularised weights along N into one
+    LDLQ traversal; distinct Hessians of one shape go through ldlq_batched.
+    Returns [(proxy, out_tensors)] per input and updates each quant_args.
+    """
+    if any("mixed_rate_axis" in a or "mixed_tile_bits" in a for a in quant_args_list):
+        raise ValueError("mixed-rate LDLQ is currently supported by quantize_qsrt, not the same-K batch API")
+    n_t = len(weights)
+    qa0 = quant_args_list[0]
+    device = torch.device(qa0["devices"][0])
+    shared_H = all(h is H_datas[0] for h in H_datas)
+    assert shared_H or all(w.shape == weights[0].shape for w in weights)
+    assert all(w.shape[0] == weights[0].shape[0] for w in weights)
+    assert all(a["K"] == qa0["K"] for a in quant_args_list)
+    results: list = [None] * n_t
+    finalized, batch = [], []
+    for t in range(n_t):
+        qa = quant_args_list[t]
+        if "seed" in qa:
+            torch.manual_seed(qa["seed"])
+        q_fallback, H, L, su, H_diag = finalize_capture_H(H_datas[t], qa, verbose)
+        if q_fallback:
+            finalized.append(None)
+        else:
+            finalized.append((H, L, su, H_diag))
+            batch.append(t)
+    for t in range(n_t):
+        if finalized[t] is None:
+            results[t] = quantize_qsrt(weights[t], H_datas[t], quant_args_list[t], False, None, verbose)[1:]
+    if not batch:
+        return results
+    regs = {}
+    for t in batch:
+        qa = quant_args_list[t]
+        if "seed" in qa:
+            torch.manual_seed(qa["seed"])
+        H, L, su, H_diag = finalized[t]
+        w = weights[t] if weights[t].device == device else weights[t].to(device)
+        su = su.to(device) if su.is_cuda else su
+        if H_diag is not None and H_diag.is_cuda:
+            H_diag = H_diag.to(device)
+        sv = output_signs(w.shape[1], device, qa)
+        apply_out, wr, _, su, sv = regularize(w, su, sv, qa, verbose, H_diag, None, skip_g_scale=True)
+        regs[t] = [wr, su, sv, apply_out]
+        weights[t] = None
+    scales = g_scale_search_batch([sample_scale_tiles(regs[t][0]) for t in batch], qa0)
+    g_scales = {}
+    for t, (g, _) in zip(batch, scales):
+        regs[t][0] *= g
+        if quant_args_list[t].get("g_scale_into_sv"):
+            regs[t][2] /= g
+        else:
+            regs[t][1] /= g
+        g_scales[t] = g
+    if shared_H:
+        L = finalized[batch[0]][1].to(device)
+        widths = [regs[t][0].shape[1] for t in batch]
+        cat = torch.cat([regs[t][0] for t in batch], dim=1)
+        for t in batch:
+            regs[t][0] = None
+        wq_cat, enc_cat = ldlq(cat, L, qa0)
+        del L
+        wrs = list(torch.split(cat, widths, dim=1))
+        wqs = list(torch.split(wq_cat, widths, dim=1))
+        encs = list(torch.split(enc_cat, [w // 16 for w in widths], dim=1))
+    else:
+        Ls = torch.stack([finalized[t][1].to(device) for t in batch])
+        stack = torch.stack([regs[t][0] for t in batch])
+        for t in batch:
+            regs[t][0] = None
+        wq_stack, enc_stack = ldlq_batched(stack, Ls, qa0)
+        del Ls
+        wrs, wqs, encs = list(stack.unbind(0)), list(wq_stack.unbind(0)), list(enc_stack.unbind(0))
+    Hd = None
+    for bi, t in enumerate(batch):
+        qa = quant_args_list[t]
+        _, su, sv, apply_out = regs[t]
+        if Hd is None or not shared_H:
+            Hd = finalized[t][0].to(device)
+        try:
+            num = block_trace(wrs[bi] - wqs[bi], Hd)
+            den = block_trace(wrs[bi], Hd)
+            proxy = num / max(den, 1e-8)
+        except torch.OutOfMemoryError:
+            proxy = -1.0
+        if qa.get("return_error_metrics") and proxy >= 0.0:
+            wr_o = _reconstruct(wrs[bi].to(device), su, sv)
+            wq_o = _reconstruct(wqs[bi].to(device), su, sv)
+            cerr = wr_o - wq_o
+            eh = qa.get("error_hessian")
+            if eh is None:
+                cnum, cden = num, den
+            else:
+                if eh.shape != (wr_o.shape[0], wr_o.shape[0]):
+                    raise ValueError("error_hessian shape does not match quantized input dimension: "
+                                     f"{eh.shape} vs {wr_o.shape[0]}")
+                eh = eh.to(device)
+                cnum, cden = block_trace(cerr, eh), block_trace(wr_o, eh)
+            qa["error_metrics"] = {"numerator": float(cnum), "denominator": float(cden),
+                                   "encoder_numerator": float(num), "encoder_denominator": float(den),
+                                   "residual_by_input": cerr.square().sum(dim=1).cpu()}
+        wrs[bi] = wqs[bi] = None
+        out = {"suh": su.flatten().contiguous().to(dtype=torch.half, copy=True),
+               "svh": sv.flatten().contiguous().to(dtype=torch.half, copy=True),
+               "trellis": pack_trellis(encs[bi].contiguous(), qa), **_codebook_tensors(qa)}
+        encs[bi] = None
+        qa.update({"apply_out_scales": apply_out, "g_scale": g_scales[t], "q_fallback": False})
+        results[t] = (proxy, out)
+    return results
+
+
+def pack_signs(signs: torch.Tensor, quant_args: dict) -> torch.Tensor:
+    """Sign-bit packing of the upstream EXL3 format (kquant/exl3_encoder_backend.py:1680-1685).
+
+    The upstream kernel is not part of the reference tree and its bit order is
+    unpinned, so this entry point refuses rather than guess a format.
+    """
+    raise NotImplementedError("pack_signs: upstream EXL3 sign packing is not pinned by the reference")

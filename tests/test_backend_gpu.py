@@ -1,0 +1,120 @@
+"""GPU tests of the plugin-API backend: closure, decode consistency, argument contracts."""
+import math
+
+import pytest
+import torch
+
+from kquant_b200 import _native, codebooks as cb
+from kquant_b200 import exl3_encoder_backend as be
+from kquant_b200.ldlq import make_shared_h
+
+pytestmark = pytest.mark.gpu
+
+
+def _problem(dev, k=256, n=512, seed=0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = torch.randn((k, n), generator=g, device=dev) * 0.02
+    x = torch.randn((4 * k, k), generator=g, device=dev) * torch.exp(torch.randn(k, generator=g, device=dev))
+    h = x.T @ x / x.shape[0]
+    return w, h
+
+
+def _args(dev, **kw):
+    a = {"K": 3, "seed": 7, "sv_seed": 11, "sigma_reg": 0.025, "devices": [str(dev)], "apply_out_scales": False,
+         "tailbite_context": 128, "sqg_e4m3_luts_by_bits": {b: cb.sqg_xor_cheb_t12_bytes(b) for b in (2, 3, 4)}}
+    a.update(kw)
+    return a
+
+
+def _decode(states, suh, svh, tile_bits, axis):
+    """Decode [k/16, n/16, 256] states with the reference decoder's maths (kquant/exl3_reference.py:146-281)."""
+    dev = states.device
+    vals = torch.empty(states.shape, dtype=torch.float32, device=dev)
+    for bits in sorted(set(tile_bits)):
+        lab = cb.sqg_codebook(bits, cb.SQG_XOR_CHEB_T12, device=dev).float()
+        v = lab[(states.long() & 0xFFFF)]
+        sel = torch.tensor([b == bits for b in tile_bits], device=dev)
+        if axis == "k":
+            vals[sel] = v[sel]
+        else:
+            vals[:, sel] = v[:, sel]
+    inv = be.tensor_core_perm_i(dev)
+    vals = vals[..., inv]
+    tk, tn, _ = vals.shape
+    w = vals.reshape(tk, tn, 16, 16).permute(0, 2, 1, 3).reshape(tk * 16, tn * 16)
+    w = be.preapply_had_l(w, 128) * suh.float().unsqueeze(1)
+    return be.preapply_had_r(w, 128) * svh.float().unsqueeze(0)
+
+
+@pytest.mark.parametrize("axis", ["n", "k"])
+def test_qsrt_batch_decodes_to_its_reconstruction(cuda_device, axis):
+    dev = cuda_device
+    w, h = _problem(dev)
+    k, n = w.shape
+    ntiles = (n if axis == "n" else k) // 16
+    bits = tuple([3] * ntiles)
+    alt = tuple((2, 3, 4)[i % 3] for i in range(ntiles))
+    groups = [[_args(dev, mixed_rate_axis=axis, mixed_tile_bits=bits), _args(dev, mixed_rate_axis=axis,
+                                                                            mixed_tile_bits=alt)]]
+    res = be.quantize_qsrt_batch([w.clone()], [make_shared_h(k, dev, h)], groups)
+    assert len(res) == 1 and len(res[0]) == 2
+    for cand, tb in zip(res[0], (bits, alt)):
+        assert math.isfinite(cand["proxy"]) and 0 < cand["proxy"] < 0.5
+        dec = _decode(cand["encoded"], cand["suh"], cand["svh"], tb, axis)
+        assert torch.allclose(dec, cand["weight_q"], atol=1e-5, rtol=0)
+        # every tile is a closed cyclic trellis path at its rate
+        for bw in set(tb):
+            sel = torch.tensor([b == bw for b in tb], device=dev)
+            st = cand["encoded"][sel] if axis == "k" else cand["encoded"][:, sel]
+            back = _native.unpack_trellis_states(_native.pack_trellis(st.contiguous(), bw), bw)
+            assert torch.equal(back, st)
+    # the all-K3 candidate of the reuse path equals a plain single-candidate encode
+    w2, h2 = _problem(dev)
+    single = be.quantize_qsrt_batch([w2], [make_shared_h(k, dev, h2)], [[_args(dev, mixed_rate_axis=axis,
+                                                                              mixed_tile_bits=bits)]])
+    assert torch.equal(single[0][0]["encoded"], res[0][0]["encoded"])
+
+
+def test_quantize_qsrt_packs_closed_trellis(cuda_device):
+    dev = cuda_device
+    w, h = _problem(dev, k=256, n=256, seed=3)
+    args = _args(dev)
+    args["sqg_e4m3_lut"] = cb.sqg_xor_cheb_t12_bytes(4)
+    del args["sqg_e4m3_luts_by_bits"]
+    args["K"] = 4
+    wq, proxy, out = be.quantize_qsrt(w.clone(), make_shared_h(256, dev, h), args, True)
+    assert out["trellis"].shape == (16, 16, 64)
+    assert out["suh"].dtype == torch.half and out["svh"].shape == (256,)
+    assert 0 < proxy < 0.1
+    assert args["q_fallback"] is False and "g_scale" in args
+    rel = (wq - w).square().sum() / w.square().sum()
+    assert rel < 0.05
+
+
+def test_uniform_batch_shared_and_distinct_h(cuda_device):
+    dev = cuda_device
+    w1, h = _problem(dev, k=256, n=256, seed=5)
+    w2, _ = _problem(dev, k=256, n=256, seed=6)
+    shared = make_shared_h(256, dev, h)
+    a1, a2 = _args(dev, seed=1, sv_seed=2), _args(dev, seed=1, sv_seed=3)
+    r = be.quantize_uniform_batch([w1.clone(), w2.clone()], [shared, shared], [a1, a2])
+    assert len(r) == 2 and all(0 < p < 0.2 for p, _ in r)
+    assert all(o["trellis"].shape == (16, 16, 48) for _, o in r)
+    hb = [make_shared_h(256, dev, h), make_shared_h(256, dev, h)]
+    r2 = be.quantize_uniform_batch([w1.clone(), w2.clone()], hb, [_args(dev, seed=1, sv_seed=2),
+                                                                  _args(dev, seed=1, sv_seed=3)])
+    assert all(0 < p < 0.2 for p, _ in r2)
+
+
+def test_quantize_tiles_dispatch_and_errors(cuda_device):
+    dev = cuda_device
+    tiles = torch.randn((5, 256), device=dev)
+    q, i = be.quantize_tiles(tiles, {"K": 2, "devices": [str(dev)], "sqg_e4m3_luts_by_bits": {2: None, 3: None, 4: None}})
+    q2, i2 = be.quantize_tiles(tiles, {"K": 2, "devices": [str(dev)], "mcg": True})
+    assert torch.equal(i, i2) and torch.equal(q, q2)
+    with pytest.raises(ValueError, match="missing rate-specific SQG K3 LUT"):
+        be.quantize_tiles(tiles, {"K": 3, "devices": [str(dev)], "sqg_e4m3_luts_by_bits": {2: None}})
+    with pytest.raises(ValueError, match="R44 mode"):
+        be.quantize_tiles(tiles, {"K": 3, "devices": [str(dev)], "sqg_e4m3_mode": "other"})
+    with pytest.raises(ValueError):
+        be.quantize_tiles(tiles[:, :255].contiguous(), {"K": 3, "devices": [str(dev)], "mcg": True})
