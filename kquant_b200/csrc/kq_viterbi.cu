@@ -31,7 +31,7 @@
 //    where tie_key orders nodes by (bitrev5(slot), bitrev5(lane), j) of the
 //    reference reduction (:330-413).
 #include <type_traits>
-#include "kq_common.cuh"
+#include "kq_viterbi_common.cuh"
 
 namespace kq {
 namespace {
@@ -39,8 +39,6 @@ namespace {
 constexpr int kThreads = 512;
 constexpr int kJobs = 2;
 constexpr int kTbThread = 0;
-
-enum Phase : int { PH_IDLE = 0, PH_FP, PH_AM, PH_TP, PH_FF, PH_TF, PH_OUT };
 
 template <int K>
 struct ThreadMap {
@@ -71,29 +69,6 @@ struct ThreadMap {
         }
     }
 };
-
-__device__ __forceinline__ uint32_t brev5(uint32_t x) { return __brev(x) >> 27; }
-
-// Tie key of node e in the reference's primer argmin order (smaller wins).
-template <int K>
-__device__ __forceinline__ uint32_t tie_key(int e) {
-    if constexpr (K == 2) {
-        const int t = e & 1023, j = e >> 10;
-        return (brev5(t >> 5) << 9) | (brev5(t & 31) << 4) | j;
-    } else {
-        const int t = e & 511, s = (e >> 9) & 1, j = e >> 10;
-        return (brev5(16 * s + (t >> 5)) << 9) | (brev5(t & 31) << 4) | j;
-    }
-}
-
-template <int K>
-__device__ __forceinline__ int key_node(uint32_t key) {
-    const int j = key & 15;
-    const int lane = brev5((key >> 4) & 31);
-    const int slot = brev5((key >> 9) & 31);
-    if constexpr (K == 2) return ((slot << 5) | lane) + (j << 10);
-    else return (((slot & 15) << 5) | lane) + ((slot >> 4) << 9) + (j << 10);
-}
 
 // One forward step of one tile.  STEP0: 0 = read cost_prev, 1 = virtual zero
 // costs (primer step 0), 2 = zero at es and +inf elsewhere (final step 0).
@@ -398,9 +373,15 @@ int launch(const float* tiles, int64_t n, const uint16_t* labels, int C, float* 
 
 }  // namespace
 
+size_t pair_decision_bytes(int K, int64_t n, int sms);
+template <int K>
+int pair_launch(const float* tiles, int64_t n, const uint16_t* labels, int C, float* vals, uint16_t* states,
+                uint8_t* ws, size_t ws_bytes, cudaStream_t stream);
+
 size_t viterbi_decision_bytes(int K, int64_t n) {
     int sms = 0;
     if (sm_count(&sms)) return 0;
+    if (K == 3 || K == 4) return pair_decision_bytes(K, n, sms);
     const int64_t grid = n <= sms ? n : sms;
     const size_t row = (K == 4) ? (size_t)kThreads * 4 : (size_t)kThreads * 8;
     return (size_t)grid * kJobs * 256 * row;
@@ -421,8 +402,8 @@ int viterbi_encode(const float* tiles, int64_t n, int K, const uint16_t* labels,
     auto* w = static_cast<uint8_t*>(ws);
     switch (K) {
     case 2: return launch<2>(tiles, n, labels, C, vals, states, w, ws_bytes, stream);
-    case 3: return launch<3>(tiles, n, labels, C, vals, states, w, ws_bytes, stream);
-    case 4: return launch<4>(tiles, n, labels, C, vals, states, w, ws_bytes, stream);
+    case 3: return pair_launch<3>(tiles, n, labels, C, vals, states, w, ws_bytes, stream);
+    case 4: return pair_launch<4>(tiles, n, labels, C, vals, states, w, ws_bytes, stream);
     default: set_error("viterbi: K must be 2, 3 or 4 (got %d)", K); return KQ_ERR_ARG;
     }
 }

@@ -1,0 +1,474 @@
+// Tile-paired tail-biting Viterbi for K3 / K4, sm_100a.
+//
+// Same recursion and tie rules as kquant/csrc/qsrt_quantize_tiles_kernel.cuh:21-471
+// (see kq_viterbi.cu for the statement).  The layout differs from the single-tile kernel:
+//
+//  * A job is a PAIR of tiles (A, B) run in lock-step.  Half2 lanes hold
+//    node pairs (2p, 2p+1), so the register-resident labels (64 half2 per
+//    thread) are used as they are.  The two tiles are two interleaved
+//    instruction streams: each thread keeps 8 independent min chains per
+//    butterfly block (4 node pairs x 2 tiles), which hides the half2
+//    pipeline latency.  Costs live in shared memory as (A, B) half2 per
+//    node: one 32-bit load per predecessor, broadcast once per tile.
+//  * Two pair-jobs are staggered per CTA when the grid is full.  Forward
+//    steps go shortest-remaining-phase first.  The four traceback chains
+//    (2 jobs x 2 tiles) are walked by lanes 0..3 of warp 0, one step per
+//    slot, with the load issued at slot start.  When no forward step is
+//    pending, the chains run to the end of their phase without slot barriers.
+//  * Decisions: 4 bits per (node, tile), one 64-bit (K4) or 128-bit (K3)
+//    word per thread per step; 32-bit sub-word (tile * G + block).
+#include "kq_viterbi_common.cuh"
+
+namespace kq {
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kJobs = 2;
+
+template <int K>
+struct PairMap {
+    static_assert(K == 3 || K == 4, "pair kernel covers K3 and K4");
+    static constexpr int NODES = 1 << (16 - K);
+    static constexpr int Q = 1 << K;
+    static constexpr int DSHIFT = 16 - 2 * K;
+    static constexpr int G = (K == 4) ? 1 : 2;        // butterfly blocks (8 nodes each) per thread
+    static constexpr int NPT = 8 * G;                 // nodes per thread
+    static constexpr int WORD_BYTES = NPT;            // 2 tiles x NPT nodes x 4 bits
+    static constexpr int ROW_BYTES = kThreads * WORD_BYTES;
+
+    __device__ static __forceinline__ int base(int tid, int g) {
+        if constexpr (K == 4) return ((tid >> 1) << 4) | ((tid & 1) << 3);
+        else return (tid + kThreads * g) << K;
+    }
+    // Owner thread, and 32-bit sub-word / nibble of node e's decision for tile t.
+    __device__ static __forceinline__ void locate(int e, int t, int& tid, int& word, int& nib) {
+        if constexpr (K == 4) {
+            tid = ((e >> 4) << 1) | ((e >> 3) & 1);
+            word = t;
+        } else {
+            const int h = e >> 3;
+            tid = h & (kThreads - 1);
+            word = t * 2 + (h >> 9);
+        }
+        nib = e & 7;
+    }
+};
+
+template <int K, bool DEC, int STEP0>
+__device__ __forceinline__ void pair_step(
+    const half2 (&L)[PairMap<K>::G][4][PairMap<K>::Q],
+    const half2* __restrict__ cprev, half2* __restrict__ cnext, half2 wA, half2 wB, int esA, int esB,
+    uint8_t* __restrict__ decrow, int tid)
+{
+    // Lanes hold node pairs (2p, 2p+1); tiles A and B are two interleaved
+    // instruction streams.  The shared (A, B) predecessor cost is loaded once
+    // per k and broadcast per tile.
+    using M = PairMap<K>;
+    const half2 zero2 = __float2half2_rn(0.f);
+    const half2 inf2 = __halves2half2(__ushort_as_half(KQ_H_INF_BITS), __ushort_as_half(KQ_H_INF_BITS));
+    uint32_t words[2 * M::G];
+#pragma unroll
+    for (int g = 0; g < M::G; ++g) {
+        const int e0 = M::base(tid, g);
+        const int h = e0 >> K;
+        half2 mnA[4], mnB[4];
+        uint32_t idA[4], idB[4];
+#pragma unroll
+        for (int k = 0; k < M::Q; ++k) {
+            const int pk = (k << M::DSHIFT) | h;
+            half2 cA, cB;
+            if constexpr (STEP0 == 0) {
+                const half2 c2 = cprev[pk];
+                cA = __low2half2(c2);
+                cB = __high2half2(c2);
+            } else if constexpr (STEP0 == 1) {
+                cA = zero2;
+                cB = zero2;
+            } else {
+                cA = (pk == esA) ? zero2 : inf2;
+                cB = (pk == esB) ? zero2 : inf2;
+            }
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const half2 dA = __hsub2(L[g][p][k], wA);
+                const half2 dB = __hsub2(L[g][p][k], wB);
+                const half2 eA = __hfma2(dA, dA, cA);
+                const half2 eB = __hfma2(dB, dB, cB);
+                if (k == 0) {
+                    mnA[p] = eA;
+                    mnB[p] = eB;
+                    if constexpr (DEC) { idA[p] = 0u; idB[p] = 0u; }
+                } else {
+                    if constexpr (DEC) {
+                        const uint32_t kk = (uint32_t)(k * 0x10001);
+                        const uint32_t ltA = __hlt2_mask(eA, mnA[p]);
+                        const uint32_t ltB = __hlt2_mask(eB, mnB[p]);
+                        idA[p] = (ltA & kk) | (~ltA & idA[p]);
+                        idB[p] = (ltB & kk) | (~ltB & idB[p]);
+                    }
+                    mnA[p] = __hmin2(eA, mnA[p]);
+                    mnB[p] = __hmin2(eB, mnB[p]);
+                }
+            }
+        }
+        // Interleave to (A, B) per node: nodes e0..e0+7 -> 8 half2 = 32 bytes.
+        uint32_t v[8];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const uint32_t a = *reinterpret_cast<uint32_t*>(&mnA[p]);
+            const uint32_t b = *reinterpret_cast<uint32_t*>(&mnB[p]);
+            v[2 * p] = __byte_perm(a, b, 0x5410);      // (A lo, B lo)
+            v[2 * p + 1] = __byte_perm(a, b, 0x7632);  // (A hi, B hi)
+        }
+        // Lanes 4..7 of each 8-lane phase store their upper half first, so a
+        // phase of 128-bit stores covers all 32 banks once.
+        uint4* dst = reinterpret_cast<uint4*>(cnext + e0);
+        const int sw = (tid >> 2) & 1;
+        const uint4 lo = make_uint4(v[0], v[1], v[2], v[3]);
+        const uint4 hi = make_uint4(v[4], v[5], v[6], v[7]);
+        dst[sw] = sw ? hi : lo;
+        dst[sw ^ 1] = sw ? lo : hi;
+        if constexpr (DEC) {
+            uint32_t a = 0, b = 0;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                a |= ((idA[p] & 0xFu) | ((idA[p] >> 12) & 0xF0u)) << (8 * p);
+                b |= ((idB[p] & 0xFu) | ((idB[p] >> 12) & 0xF0u)) << (8 * p);
+            }
+            words[g] = a;
+            words[M::G + g] = b;
+        }
+    }
+    if constexpr (DEC) {
+        if constexpr (M::G == 1) {
+            __stcs(reinterpret_cast<unsigned long long*>(decrow) + tid,
+                   (unsigned long long)words[0] | ((unsigned long long)words[1] << 32));
+        } else {
+            __stcs(reinterpret_cast<uint4*>(decrow) + tid, make_uint4(words[0], words[1], words[2], words[3]));
+        }
+    }
+}
+
+// Traceback lane state: lanes 0..2*kJobs-1 of warp 0 walk chain (job, tile).
+struct TbLane {
+    int node;
+    int row;
+};
+
+// S consecutive forward steps of job F (one template variant for the run),
+// with one traceback step per forward step for every chain in a traceback
+// phase.  Control decisions are made only between runs.
+template <int K, bool DEC, int STEP0>
+__device__ __forceinline__ void run_steps(
+    const half2 (&L)[PairMap<K>::G][4][PairMap<K>::Q], half2* cost_job, int& par, const half2* wsh_job,
+    int ri, int S, int esA, int esB, uint8_t* dec_job, int tid,
+    bool tb_on, bool tb_final, TbLane& tb, const uint8_t* tb_dec, int tb_tile, uint16_t* tb_enc)
+{
+    using M = PairMap<K>;
+    for (int s = 0; s < S; ++s) {
+        unsigned int tbw = 0;
+        if (tb_on) {
+            int owner, word, nib;
+            M::locate(tb.node, tb_tile, owner, word, nib);
+            tbw = __ldcg(reinterpret_cast<const unsigned int*>(tb_dec + (size_t)tb.row * M::ROW_BYTES +
+                                                              (size_t)owner * M::WORD_BYTES) + word);
+        }
+        const half2 w2 = wsh_job[ri];
+        pair_step<K, DEC, STEP0>(L, cost_job + par * M::NODES, cost_job + (par ^ 1) * M::NODES,
+                                 __low2half2(w2), __high2half2(w2), esA, esB,
+                                 dec_job + (size_t)ri * M::ROW_BYTES, tid);
+        if (tb_on) {
+            int owner, word, nib;
+            M::locate(tb.node, tb_tile, owner, word, nib);
+            const int d = (int)((tbw >> (4 * nib)) & (M::Q - 1));
+            if (tb_final) tb_enc[tb.row] = (uint16_t)((d << (16 - K)) | tb.node);
+            tb.node = (d << M::DSHIFT) | (tb.node >> K);
+            --tb.row;
+        }
+        par ^= 1;
+        ri = (ri + 1) & 255;
+        __syncthreads();
+    }
+}
+
+template <int K>
+__global__ void __launch_bounds__(kThreads, 1)
+pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __restrict__ labels32,
+            const __half* __restrict__ labels16, int C, int njobs,
+            float* __restrict__ out_vals, uint16_t* __restrict__ out_states, uint8_t* __restrict__ decisions)
+{
+    using M = PairMap<K>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    half2* cost = reinterpret_cast<half2*>(smem);                       // [kJobs][2][NODES]
+    half2* wsh = cost + kJobs * 2 * M::NODES;                           // [kJobs][256] (A, B)
+    uint16_t* enc = reinterpret_cast<uint16_t*>(wsh + kJobs * 256);     // [kJobs][2][256]
+    uint32_t* red = reinterpret_cast<uint32_t*>(enc + kJobs * 2 * 256); // [kJobs][2][16]
+    int* es_sh = reinterpret_cast<int*>(red + kJobs * 2 * 16);          // [kJobs][2]
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int64_t n_pairs = (n_tiles + 1) >> 1;
+    const bool tb_lane = (warp == 0) && (lane < 2 * kJobs);
+    const int tb_job = (lane >> 1) & (kJobs - 1), tb_tile = lane & 1;
+
+    half2 L[M::G][4][M::Q];
+#pragma unroll
+    for (int g = 0; g < M::G; ++g)
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+#pragma unroll
+            for (int k = 0; k < M::Q; ++k) {
+                const uint32_t t = ((uint32_t)k << (16 - K)) | (uint32_t)(M::base(tid, g) + 2 * p);
+                const uint32_t v = __ldg(labels32 + (t >> 1));
+                L[g][p][k] = *reinterpret_cast<const half2*>(&v);
+            }
+
+    uint8_t* dec_base = decisions + (size_t)blockIdx.x * kJobs * 256 * M::ROW_BYTES;
+    auto dec_job = [&](int j) { return dec_base + (size_t)j * 256 * M::ROW_BYTES; };
+    auto load_pair = [&](int j, int64_t q) {
+        const int t = tid >> 8, r = tid & 255;
+        int64_t tile = 2 * q + t;
+        if (tile >= n_tiles) tile = 2 * q;
+        reinterpret_cast<__half*>(wsh + j * 256 + r)[t] = __float2half_rn(tiles[tile * 256 + r]);
+    };
+
+    int phase[kJobs], step[kJobs], par[kJobs];
+    int64_t pair[kJobs];
+    int64_t taken = 0;
+    TbLane tb{0, 0};
+#pragma unroll
+    for (int j = 0; j < kJobs; ++j) {
+        const int64_t q = (int64_t)blockIdx.x + (int64_t)gridDim.x * taken;
+        pair[j] = q;
+        step[j] = 0;
+        par[j] = 0;
+        if (j < njobs && q < n_pairs) {
+            phase[j] = PH_FP;
+            ++taken;
+            load_pair(j, q);
+        } else {
+            phase[j] = PH_IDLE;
+        }
+    }
+    __syncthreads();
+
+    while (true) {
+        bool any = false, ctrl = false;
+#pragma unroll
+        for (int j = 0; j < kJobs; ++j) {
+            any |= (phase[j] != PH_IDLE);
+            ctrl |= (phase[j] == PH_AM) || (phase[j] == PH_OUT);
+        }
+        if (!any) break;
+
+        if (ctrl) {
+            // Control slot: primer argmin and tile output / refill.
+            int64_t qnext[kJobs];
+            int64_t cnt = taken;
+#pragma unroll
+            for (int j = 0; j < kJobs; ++j) {
+                qnext[j] = n_pairs;
+                if (phase[j] == PH_OUT) {
+                    const int64_t q = (int64_t)blockIdx.x + (int64_t)gridDim.x * cnt;
+                    if (q < n_pairs) { qnext[j] = q; ++cnt; }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kJobs; ++j) {
+                if (phase[j] == PH_AM) {
+                    // Argmin over the second-to-last primer step (the reference's buffer quirk).
+                    const half2* c = cost + (j * 2 + (par[j] ^ 1)) * M::NODES;
+                    uint32_t bA = 0xFFFFFFFFu, bB = 0xFFFFFFFFu;
+#pragma unroll
+                    for (int g = 0; g < M::G; ++g)
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const int e = M::base(tid, g) + q;
+                            const uint32_t bits = *reinterpret_cast<const uint32_t*>(c + e);
+                            const uint32_t key = tie_key<K>(e);
+                            bA = min(bA, (bits << 16) | key);
+                            bB = min(bB, (bits & 0xFFFF0000u) | key);
+                        }
+                    bA = __reduce_min_sync(0xFFFFFFFFu, bA);
+                    bB = __reduce_min_sync(0xFFFFFFFFu, bB);
+                    if (lane == 0) {
+                        red[(j * 2 + 0) * 16 + warp] = bA;
+                        red[(j * 2 + 1) * 16 + warp] = bB;
+                    }
+                } else if (phase[j] == PH_OUT) {
+                    const int t = tid >> 8, r = tid & 255;
+                    const int64_t tile = 2 * pair[j] + t;
+                    if (tile < n_tiles) {
+                        const uint16_t sv = enc[(j * 2 + t) * 256 + r];
+                        out_states[tile * 256 + r] = sv;
+                        out_vals[tile * 256 + r] = __half2float(labels16[sv]);
+                    }
+                    if (qnext[j] < n_pairs) load_pair(j, qnext[j]);
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < kJobs; ++j) {
+                if (phase[j] == PH_AM) {
+                    phase[j] = PH_TP;
+                    step[j] = 0;
+                    if (tb_lane && tb_job == j) {
+                        uint32_t best = 0xFFFFFFFFu;
+                        for (int w = 0; w < kThreads / 32; ++w) best = min(best, red[(j * 2 + tb_tile) * 16 + w]);
+                        tb.node = key_node<K>(best & 0xFFFFu);
+                        tb.row = C - 1;
+                    }
+                } else if (phase[j] == PH_OUT) {
+                    if (qnext[j] < n_pairs) { pair[j] = qnext[j]; ++taken; phase[j] = PH_FP; }
+                    else phase[j] = PH_IDLE;
+                    step[j] = 0;
+                    par[j] = 0;
+                }
+            }
+            continue;
+        }
+
+        // Forward job (shortest remaining forward phase first) and run length.
+        int F = -1, F_rem = 1 << 30;
+#pragma unroll
+        for (int j = 0; j < kJobs; ++j) {
+            if (phase[j] == PH_FP || phase[j] == PH_FF) {
+                const int rem = (phase[j] == PH_FP ? 2 * C : 256) - step[j];
+                if (rem < F_rem) { F_rem = rem; F = j; }
+            }
+        }
+        const int my_phase = phase[tb_job];
+        const bool my_tb = tb_lane && (my_phase == PH_TP || my_phase == PH_TF);
+        const uint8_t* my_dec = dec_job(tb_job);
+        uint16_t* my_enc = enc + (tb_job * 2 + tb_tile) * 256;
+
+        if (F < 0) {
+            // Every active job is in a traceback phase: walk to the phase ends without barriers.
+            if (my_tb) {
+                const int steps = (my_phase == PH_TP) ? C - step[tb_job] : 256 - step[tb_job];
+                for (int s = 0; s < steps; ++s) {
+                    int owner, word, nib;
+                    M::locate(tb.node, tb_tile, owner, word, nib);
+                    const unsigned int w = __ldcg(reinterpret_cast<const unsigned int*>(
+                        my_dec + (size_t)tb.row * M::ROW_BYTES + (size_t)owner * M::WORD_BYTES) + word);
+                    const int d = (int)((w >> (4 * nib)) & (M::Q - 1));
+                    if (my_phase == PH_TF) my_enc[tb.row] = (uint16_t)((d << (16 - K)) | tb.node);
+                    tb.node = (d << M::DSHIFT) | (tb.node >> K);
+                    --tb.row;
+                }
+                if (my_phase == PH_TP) {
+                    es_sh[tb_job * 2 + tb_tile] = tb.node;
+                    tb.row = 255;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < kJobs; ++j) {
+                if (phase[j] == PH_TP) { phase[j] = PH_FF; step[j] = 0; }
+                else if (phase[j] == PH_TF) { phase[j] = PH_OUT; step[j] = 0; }
+            }
+            continue;
+        }
+
+        const int ph = phase[F], i0 = step[F];
+        int S = F_rem;
+        if (ph == PH_FP && i0 < C) S = C - i0;           // decision-free part of the primer
+        if (i0 == 0) S = 1;                               // step 0 has its own variant
+#pragma unroll
+        for (int j = 0; j < kJobs; ++j) {
+            if (j != F && phase[j] == PH_TP) S = min(S, C - step[j]);
+            if (j != F && phase[j] == PH_TF) S = min(S, 256 - step[j]);
+        }
+        const int ri0 = (ph == PH_FP) ? ((i0 + 256 - C) & 255) : i0;
+        const bool run_tb = my_tb && (tb_job != F);
+        const bool tb_final = (my_phase == PH_TF);
+        half2* cj = cost + F * 2 * M::NODES;
+        int pF = par[F];
+        if (i0 == 0) {
+            if (ph == PH_FP)
+                run_steps<K, false, 1>(L, cj, pF, wsh + F * 256, ri0, S, 0, 0, dec_job(F), tid, run_tb, tb_final, tb,
+                                       my_dec, tb_tile, my_enc);
+            else
+                run_steps<K, true, 2>(L, cj, pF, wsh + F * 256, ri0, S, es_sh[F * 2], es_sh[F * 2 + 1], dec_job(F),
+                                      tid, run_tb, tb_final, tb, my_dec, tb_tile, my_enc);
+        } else if (ph == PH_FF || i0 >= C) {
+            run_steps<K, true, 0>(L, cj, pF, wsh + F * 256, ri0, S, 0, 0, dec_job(F), tid, run_tb, tb_final, tb,
+                                  my_dec, tb_tile, my_enc);
+        } else {
+            run_steps<K, false, 0>(L, cj, pF, wsh + F * 256, ri0, S, 0, 0, dec_job(F), tid, run_tb, tb_final, tb,
+                                   my_dec, tb_tile, my_enc);
+        }
+        // Chains that finished their primer traceback publish the end state.
+        if (run_tb && my_phase == PH_TP && step[tb_job] + S == C) {
+            es_sh[tb_job * 2 + tb_tile] = tb.node;
+            tb.row = 255;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kJobs; ++j) {
+            if (j == F) {
+                par[j] = pF;
+                step[j] += S;
+                if (phase[j] == PH_FP && step[j] == 2 * C) { phase[j] = PH_AM; step[j] = 0; }
+                else if (phase[j] == PH_FF && step[j] == 256) { phase[j] = PH_TF; step[j] = 0; }
+            } else if (phase[j] == PH_TP) {
+                step[j] += S;
+                if (step[j] == C) { phase[j] = PH_FF; step[j] = 0; }
+            } else if (phase[j] == PH_TF) {
+                step[j] += S;
+                if (step[j] == 256) { phase[j] = PH_OUT; step[j] = 0; }
+            }
+        }
+    }
+}
+
+template <int K>
+constexpr size_t pair_smem_bytes() {
+    return (size_t)kJobs * 2 * PairMap<K>::NODES * 4 + kJobs * 256 * 4 + kJobs * 2 * 256 * 2 + kJobs * 2 * 16 * 4 +
+           kJobs * 2 * 4;
+}
+
+template <int K>
+void pair_grid(int64_t n, int sms, int& grid, int& njobs) {
+    const int64_t pairs = (n + 1) / 2;
+    if (pairs <= sms) { grid = (int)pairs; njobs = 1; }
+    else { grid = sms; njobs = kJobs; }
+}
+
+}  // namespace
+
+size_t pair_decision_bytes(int K, int64_t n, int sms) {
+    int grid, nj;
+    if (K == 4) pair_grid<4>(n, sms, grid, nj);
+    else pair_grid<3>(n, sms, grid, nj);
+    const size_t row = (K == 4) ? PairMap<4>::ROW_BYTES : PairMap<3>::ROW_BYTES;
+    return (size_t)grid * kJobs * 256 * row;
+}
+
+template <int K>
+int pair_launch(const float* tiles, int64_t n, const uint16_t* labels, int C, float* vals, uint16_t* states,
+                uint8_t* ws, size_t ws_bytes, cudaStream_t stream) {
+    int sms = 0;
+    if (int rc = sm_count(&sms)) return rc;
+    int grid, njobs;
+    pair_grid<K>(n, sms, grid, njobs);
+    const size_t need = (size_t)grid * kJobs * 256 * PairMap<K>::ROW_BYTES;
+    if (ws_bytes < need) {
+        set_error("viterbi workspace too small: %zu < %zu", ws_bytes, need);
+        return KQ_ERR_WORKSPACE;
+    }
+    const size_t sm = pair_smem_bytes<K>();
+    cudaError_t e = cudaFuncSetAttribute(pair_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
+    pair_kernel<K><<<grid, kThreads, sm, stream>>>(tiles, n, reinterpret_cast<const uint32_t*>(labels),
+                                                   reinterpret_cast<const __half*>(labels), C, njobs, vals, states,
+                                                   ws);
+    return check_launch("pair_kernel");
+}
+
+template int pair_launch<3>(const float*, int64_t, const uint16_t*, int, float*, uint16_t*, uint8_t*, size_t,
+                            cudaStream_t);
+template int pair_launch<4>(const float*, int64_t, const uint16_t*, int, float*, uint16_t*, uint8_t*, size_t,
+                            cudaStream_t);
+
+}  // namespace kq
