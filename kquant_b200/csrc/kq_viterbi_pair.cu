@@ -1,4 +1,4 @@
-// Tile-paired tail-biting Viterbi for K3 / K4, sm_100a.
+// Tile-paired tail-biting Viterbi for K2 / K3 / K4, sm_100a.
 //
 // Same recursion and tie rules as kquant/csrc/qsrt_quantize_tiles_kernel.cuh:21-471
 // (see kq_viterbi.cu for the statement).  The layout differs from the single-tile kernel:
@@ -15,8 +15,12 @@
 //    (2 jobs x 2 tiles) are walked by lanes 0..3 of warp 0, one step per
 //    slot, with the load issued at slot start.  When no forward step is
 //    pending, the chains run to the end of their phase without slot barriers.
-//  * Decisions: 4 bits per (node, tile), one 64-bit (K4) or 128-bit (K3)
-//    word per thread per step; 32-bit sub-word (tile * G + block).
+//  * Decisions: 4 bits (K3, K4) or 2 bits (K2) per (node, tile), one 64-bit
+//    (K4) or 128-bit (K2, K3) word per thread per step, tile A's bits first.
+//  * One (A, B) cost double buffer per CTA: forward phases never preempt
+//    one another, and a job's traceback phase (C or 256 steps) never
+//    outlasts the other job's forward phase (2C or 256 steps), so the stagger
+//    keeps the ALU busy without a second buffer.
 #include "kq_viterbi_common.cuh"
 
 namespace kq {
@@ -27,36 +31,45 @@ constexpr int kJobs = 2;
 
 template <int K>
 struct PairMap {
-    static_assert(K == 3 || K == 4, "pair kernel covers K3 and K4");
+    static_assert(K >= 2 && K <= 4, "pair kernel covers K2..K4");
     static constexpr int NODES = 1 << (16 - K);
     static constexpr int Q = 1 << K;
     static constexpr int DSHIFT = 16 - 2 * K;
-    static constexpr int G = (K == 4) ? 1 : 2;        // butterfly blocks (8 nodes each) per thread
-    static constexpr int NPT = 8 * G;                 // nodes per thread
-    static constexpr int WORD_BYTES = NPT;            // 2 tiles x NPT nodes x 4 bits
+    static constexpr int PB = (K == 2) ? 2 : 4;             // node pairs per block part
+    static constexpr int G = (K == 4) ? 1 : (K == 3 ? 2 : 8);   // block parts per thread
+    static constexpr int NPT = 2 * PB * G;                  // nodes per thread (8, 16, 32)
+    static constexpr int DB = (K == 2) ? 2 : 4;             // decision bits per (node, tile)
+    static constexpr int TILE_WORDS = NPT * DB / 32;        // 32-bit words per tile per thread
+    static constexpr int WORD_BYTES = 2 * TILE_WORDS * 4;   // both tiles
     static constexpr int ROW_BYTES = kThreads * WORD_BYTES;
 
+    // First node of block part g of thread tid (even; 16-byte aligned as (A, B) half2).
     __device__ static __forceinline__ int base(int tid, int g) {
         if constexpr (K == 4) return ((tid >> 1) << 4) | ((tid & 1) << 3);
         else return (tid + kThreads * g) << K;
     }
-    // Owner thread, and 32-bit sub-word / nibble of node e's decision for tile t.
-    __device__ static __forceinline__ void locate(int e, int t, int& tid, int& word, int& nib) {
+    // Owner thread, 32-bit word and bit shift of node e's decision for tile t.
+    __device__ static __forceinline__ void locate(int e, int t, int& tid, int& word, int& shift) {
+        int g, j;
         if constexpr (K == 4) {
             tid = ((e >> 4) << 1) | ((e >> 3) & 1);
-            word = t;
+            g = 0;
+            j = e & 7;
         } else {
-            const int h = e >> 3;
+            const int h = e >> K;
             tid = h & (kThreads - 1);
-            word = t * 2 + (h >> 9);
+            g = h >> 9;
+            j = e & (2 * PB - 1);
         }
-        nib = e & 7;
+        const int bit = (g * 2 * PB + j) * DB;
+        word = t * TILE_WORDS + (bit >> 5);
+        shift = bit & 31;
     }
 };
 
 template <int K, bool DEC, int STEP0>
 __device__ __forceinline__ void pair_step(
-    const half2 (&L)[PairMap<K>::G][4][PairMap<K>::Q],
+    const half2 (&L)[PairMap<K>::G][PairMap<K>::PB][PairMap<K>::Q],
     const half2* __restrict__ cprev, half2* __restrict__ cnext, half2 wA, half2 wB, int esA, int esB,
     uint8_t* __restrict__ decrow, int tid)
 {
@@ -64,15 +77,18 @@ __device__ __forceinline__ void pair_step(
     // instruction streams.  The shared (A, B) predecessor cost is loaded once
     // per k and broadcast per tile.
     using M = PairMap<K>;
+    constexpr int PB = M::PB;
     const half2 zero2 = __float2half2_rn(0.f);
     const half2 inf2 = __halves2half2(__ushort_as_half(KQ_H_INF_BITS), __ushort_as_half(KQ_H_INF_BITS));
-    uint32_t words[2 * M::G];
+    uint32_t words[2 * M::TILE_WORDS];
+#pragma unroll
+    for (int w = 0; w < 2 * M::TILE_WORDS; ++w) words[w] = 0;
 #pragma unroll
     for (int g = 0; g < M::G; ++g) {
         const int e0 = M::base(tid, g);
         const int h = e0 >> K;
-        half2 mnA[4], mnB[4];
-        uint32_t idA[4], idB[4];
+        half2 mnA[PB], mnB[PB];
+        uint32_t idA[PB], idB[PB];
 #pragma unroll
         for (int k = 0; k < M::Q; ++k) {
             const int pk = (k << M::DSHIFT) | h;
@@ -89,7 +105,7 @@ __device__ __forceinline__ void pair_step(
                 cB = (pk == esB) ? zero2 : inf2;
             }
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
+            for (int p = 0; p < PB; ++p) {
                 const half2 dA = __hsub2(L[g][p][k], wA);
                 const half2 dB = __hsub2(L[g][p][k], wB);
                 const half2 eA = __hfma2(dA, dA, cA);
@@ -111,36 +127,40 @@ __device__ __forceinline__ void pair_step(
                 }
             }
         }
-        // Interleave to (A, B) per node: nodes e0..e0+7 -> 8 half2 = 32 bytes.
-        uint32_t v[8];
+        // Interleave to (A, B) per node and store 2*PB half2 (16 or 32 bytes).
+        uint32_t v[2 * PB];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
+        for (int p = 0; p < PB; ++p) {
             const uint32_t a = *reinterpret_cast<uint32_t*>(&mnA[p]);
             const uint32_t b = *reinterpret_cast<uint32_t*>(&mnB[p]);
             v[2 * p] = __byte_perm(a, b, 0x5410);      // (A lo, B lo)
             v[2 * p + 1] = __byte_perm(a, b, 0x7632);  // (A hi, B hi)
         }
-        // Lanes 4..7 of each 8-lane phase store their upper half first, so a
-        // phase of 128-bit stores covers all 32 banks once.
         uint4* dst = reinterpret_cast<uint4*>(cnext + e0);
-        const int sw = (tid >> 2) & 1;
-        const uint4 lo = make_uint4(v[0], v[1], v[2], v[3]);
-        const uint4 hi = make_uint4(v[4], v[5], v[6], v[7]);
-        dst[sw] = sw ? hi : lo;
-        dst[sw ^ 1] = sw ? lo : hi;
+        if constexpr (PB == 4) {
+            // Lanes 4..7 of each 8-lane phase store their upper half first, so
+            // a phase of 128-bit stores covers all 32 banks once.
+            const int sw = (tid >> 2) & 1;
+            const uint4 lo = make_uint4(v[0], v[1], v[2], v[3]);
+            const uint4 hi = make_uint4(v[4], v[5], v[6], v[7]);
+            dst[sw] = sw ? hi : lo;
+            dst[sw ^ 1] = sw ? lo : hi;
+        } else {
+            dst[0] = make_uint4(v[0], v[1], v[2], v[3]);
+        }
         if constexpr (DEC) {
-            uint32_t a = 0, b = 0;
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
-                a |= ((idA[p] & 0xFu) | ((idA[p] >> 12) & 0xF0u)) << (8 * p);
-                b |= ((idB[p] & 0xFu) | ((idB[p] >> 12) & 0xF0u)) << (8 * p);
+            for (int p = 0; p < PB; ++p) {
+                const int bit = (g * 2 * PB + 2 * p) * M::DB;
+                const uint32_t a = (idA[p] & 0xFFFFu) | ((idA[p] >> 16) << M::DB);
+                const uint32_t b = (idB[p] & 0xFFFFu) | ((idB[p] >> 16) << M::DB);
+                words[bit >> 5] |= a << (bit & 31);
+                words[M::TILE_WORDS + (bit >> 5)] |= b << (bit & 31);
             }
-            words[g] = a;
-            words[M::G + g] = b;
         }
     }
     if constexpr (DEC) {
-        if constexpr (M::G == 1) {
+        if constexpr (M::TILE_WORDS == 1) {
             __stcs(reinterpret_cast<unsigned long long*>(decrow) + tid,
                    (unsigned long long)words[0] | ((unsigned long long)words[1] << 32));
         } else {
@@ -160,7 +180,7 @@ struct TbLane {
 // phase.  Control decisions are made only between runs.
 template <int K, bool DEC, int STEP0>
 __device__ __forceinline__ void run_steps(
-    const half2 (&L)[PairMap<K>::G][4][PairMap<K>::Q], half2* cost_job, int& par, const half2* wsh_job,
+    const half2 (&L)[PairMap<K>::G][PairMap<K>::PB][PairMap<K>::Q], half2* cost_job, int& par, const half2* wsh_job,
     int ri, int S, int esA, int esB, uint8_t* dec_job, int tid,
     bool tb_on, bool tb_final, TbLane& tb, const uint8_t* tb_dec, int tb_tile, uint16_t* tb_enc)
 {
@@ -168,8 +188,8 @@ __device__ __forceinline__ void run_steps(
     for (int s = 0; s < S; ++s) {
         unsigned int tbw = 0;
         if (tb_on) {
-            int owner, word, nib;
-            M::locate(tb.node, tb_tile, owner, word, nib);
+            int owner, word, sh;
+            M::locate(tb.node, tb_tile, owner, word, sh);
             tbw = __ldcg(reinterpret_cast<const unsigned int*>(tb_dec + (size_t)tb.row * M::ROW_BYTES +
                                                               (size_t)owner * M::WORD_BYTES) + word);
         }
@@ -178,9 +198,9 @@ __device__ __forceinline__ void run_steps(
                                  __low2half2(w2), __high2half2(w2), esA, esB,
                                  dec_job + (size_t)ri * M::ROW_BYTES, tid);
         if (tb_on) {
-            int owner, word, nib;
-            M::locate(tb.node, tb_tile, owner, word, nib);
-            const int d = (int)((tbw >> (4 * nib)) & (M::Q - 1));
+            int owner, word, sh;
+            M::locate(tb.node, tb_tile, owner, word, sh);
+            const int d = (int)((tbw >> sh) & (M::Q - 1));
             if (tb_final) tb_enc[tb.row] = (uint16_t)((d << (16 - K)) | tb.node);
             tb.node = (d << M::DSHIFT) | (tb.node >> K);
             --tb.row;
@@ -199,8 +219,10 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
 {
     using M = PairMap<K>;
     extern __shared__ __align__(16) uint8_t smem[];
-    half2* cost = reinterpret_cast<half2*>(smem);                       // [kJobs][2][NODES]
-    half2* wsh = cost + kJobs * 2 * M::NODES;                           // [kJobs][256] (A, B)
+    // One (A, B) cost double buffer shared by the jobs: forward phases are
+    // non-preemptive, so at most one job is between forward steps at a time.
+    half2* cost = reinterpret_cast<half2*>(smem);                       // [2][NODES]
+    half2* wsh = cost + 2 * M::NODES;                                   // [kJobs][256] (A, B)
     uint16_t* enc = reinterpret_cast<uint16_t*>(wsh + kJobs * 256);     // [kJobs][2][256]
     uint32_t* red = reinterpret_cast<uint32_t*>(enc + kJobs * 2 * 256); // [kJobs][2][16]
     int* es_sh = reinterpret_cast<int*>(red + kJobs * 2 * 16);          // [kJobs][2]
@@ -211,11 +233,11 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
     const bool tb_lane = (warp == 0) && (lane < 2 * kJobs);
     const int tb_job = (lane >> 1) & (kJobs - 1), tb_tile = lane & 1;
 
-    half2 L[M::G][4][M::Q];
+    half2 L[M::G][M::PB][M::Q];
 #pragma unroll
     for (int g = 0; g < M::G; ++g)
 #pragma unroll
-        for (int p = 0; p < 4; ++p)
+        for (int p = 0; p < M::PB; ++p)
 #pragma unroll
             for (int k = 0; k < M::Q; ++k) {
                 const uint32_t t = ((uint32_t)k << (16 - K)) | (uint32_t)(M::base(tid, g) + 2 * p);
@@ -277,12 +299,12 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
             for (int j = 0; j < kJobs; ++j) {
                 if (phase[j] == PH_AM) {
                     // Argmin over the second-to-last primer step (the reference's buffer quirk).
-                    const half2* c = cost + (j * 2 + (par[j] ^ 1)) * M::NODES;
+                    const half2* c = cost + (par[j] ^ 1) * M::NODES;
                     uint32_t bA = 0xFFFFFFFFu, bB = 0xFFFFFFFFu;
 #pragma unroll
                     for (int g = 0; g < M::G; ++g)
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
+                        for (int q = 0; q < 2 * M::PB; ++q) {
                             const int e = M::base(tid, g) + q;
                             const uint32_t bits = *reinterpret_cast<const uint32_t*>(c + e);
                             const uint32_t key = tie_key<K>(e);
@@ -328,16 +350,20 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
             continue;
         }
 
-        // Forward job (shortest remaining forward phase first) and run length.
-        int F = -1, F_rem = 1 << 30;
+        // Forward job: a job inside a forward phase keeps it (the cost buffer is
+        // shared); otherwise the ready job with the shortest phase goes first.
+        int F = -1, F_rem = 0, F_key = 1 << 30;
 #pragma unroll
         for (int j = 0; j < kJobs; ++j) {
             if (phase[j] == PH_FP || phase[j] == PH_FF) {
                 const int rem = (phase[j] == PH_FP ? 2 * C : 256) - step[j];
-                if (rem < F_rem) { F_rem = rem; F = j; }
+                const int key = step[j] > 0 ? -1 : rem;
+                if (key < F_key) { F_key = key; F_rem = rem; F = j; }
             }
         }
-        const int my_phase = phase[tb_job];
+        static_assert(kJobs == 2, "job selection below assumes two jobs");
+        const int my_phase = tb_job ? phase[1] : phase[0];
+        const int my_step = tb_job ? step[1] : step[0];
         const bool my_tb = tb_lane && (my_phase == PH_TP || my_phase == PH_TF);
         const uint8_t* my_dec = dec_job(tb_job);
         uint16_t* my_enc = enc + (tb_job * 2 + tb_tile) * 256;
@@ -345,13 +371,13 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
         if (F < 0) {
             // Every active job is in a traceback phase: walk to the phase ends without barriers.
             if (my_tb) {
-                const int steps = (my_phase == PH_TP) ? C - step[tb_job] : 256 - step[tb_job];
+                const int steps = (my_phase == PH_TP) ? C - my_step : 256 - my_step;
                 for (int s = 0; s < steps; ++s) {
-                    int owner, word, nib;
-                    M::locate(tb.node, tb_tile, owner, word, nib);
+                    int owner, word, sh;
+                    M::locate(tb.node, tb_tile, owner, word, sh);
                     const unsigned int w = __ldcg(reinterpret_cast<const unsigned int*>(
                         my_dec + (size_t)tb.row * M::ROW_BYTES + (size_t)owner * M::WORD_BYTES) + word);
-                    const int d = (int)((w >> (4 * nib)) & (M::Q - 1));
+                    const int d = (int)((w >> sh) & (M::Q - 1));
                     if (my_phase == PH_TF) my_enc[tb.row] = (uint16_t)((d << (16 - K)) | tb.node);
                     tb.node = (d << M::DSHIFT) | (tb.node >> K);
                     --tb.row;
@@ -370,7 +396,8 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
             continue;
         }
 
-        const int ph = phase[F], i0 = step[F];
+        const int ph = F ? phase[1] : phase[0];
+        const int i0 = F ? step[1] : step[0];
         int S = F_rem;
         if (ph == PH_FP && i0 < C) S = C - i0;           // decision-free part of the primer
         if (i0 == 0) S = 1;                               // step 0 has its own variant
@@ -382,8 +409,8 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
         const int ri0 = (ph == PH_FP) ? ((i0 + 256 - C) & 255) : i0;
         const bool run_tb = my_tb && (tb_job != F);
         const bool tb_final = (my_phase == PH_TF);
-        half2* cj = cost + F * 2 * M::NODES;
-        int pF = par[F];
+        half2* cj = cost;
+        int pF = F ? par[1] : par[0];
         if (i0 == 0) {
             if (ph == PH_FP)
                 run_steps<K, false, 1>(L, cj, pF, wsh + F * 256, ri0, S, 0, 0, dec_job(F), tid, run_tb, tb_final, tb,
@@ -399,7 +426,7 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
                                    my_dec, tb_tile, my_enc);
         }
         // Chains that finished their primer traceback publish the end state.
-        if (run_tb && my_phase == PH_TP && step[tb_job] + S == C) {
+        if (run_tb && my_phase == PH_TP && my_step + S == C) {
             es_sh[tb_job * 2 + tb_tile] = tb.node;
             tb.row = 255;
         }
@@ -424,7 +451,7 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
 
 template <int K>
 constexpr size_t pair_smem_bytes() {
-    return (size_t)kJobs * 2 * PairMap<K>::NODES * 4 + kJobs * 256 * 4 + kJobs * 2 * 256 * 2 + kJobs * 2 * 16 * 4 +
+    return (size_t)2 * PairMap<K>::NODES * 4 + kJobs * 256 * 4 + kJobs * 2 * 256 * 2 + kJobs * 2 * 16 * 4 +
            kJobs * 2 * 4;
 }
 
@@ -439,9 +466,8 @@ void pair_grid(int64_t n, int sms, int& grid, int& njobs) {
 
 size_t pair_decision_bytes(int K, int64_t n, int sms) {
     int grid, nj;
-    if (K == 4) pair_grid<4>(n, sms, grid, nj);
-    else pair_grid<3>(n, sms, grid, nj);
-    const size_t row = (K == 4) ? PairMap<4>::ROW_BYTES : PairMap<3>::ROW_BYTES;
+    pair_grid<3>(n, sms, grid, nj);
+    const size_t row = (K == 4) ? PairMap<4>::ROW_BYTES : (K == 3 ? PairMap<3>::ROW_BYTES : PairMap<2>::ROW_BYTES);
     return (size_t)grid * kJobs * 256 * row;
 }
 
@@ -466,6 +492,8 @@ int pair_launch(const float* tiles, int64_t n, const uint16_t* labels, int C, fl
     return check_launch("pair_kernel");
 }
 
+template int pair_launch<2>(const float*, int64_t, const uint16_t*, int, float*, uint16_t*, uint8_t*, size_t,
+                            cudaStream_t);
 template int pair_launch<3>(const float*, int64_t, const uint16_t*, int, float*, uint16_t*, uint8_t*, size_t,
                             cudaStream_t);
 template int pair_launch<4>(const float*, int64_t, const uint16_t*, int, float*, uint16_t*, uint8_t*, size_t,
