@@ -113,6 +113,24 @@ int kq_unpack_trellis_states(const uint16_t* packed, int64_t n_tiles, int K, uin
                              void* stream);
 
 /*
+ * Allocation-free variant of kq_quantize_tiles_sqg for callers that cannot
+ * allocate device memory themselves (a host whose allocator owns every byte
+ * of the device, or code that must not trigger an allocation at an arbitrary
+ * point).  No counterpart in the reference.  Same inputs, outputs and
+ * results as kq_quantize_tiles_sqg, but no workspace argument: its scratch
+ * (label table + decision rows, 32 MiB + 128 KiB) is a fixed __device__
+ * array that every GPU loading this library holds until exit.  At most
+ * KQ_NOALLOC_MAX_TILES tiles per call; larger counts return KQ_ERR_ARG.
+ * The first call on a device resolves the scratch address for that device;
+ * make that call before any stream capture.  All calls share one scratch:
+ * calls that overlap on the GPU (different streams, or different host
+ * threads) race and corrupt each other's results; serialize them.
+ */
+#define KQ_NOALLOC_MAX_TILES 4096
+int kq_quantize_tiles_sqg_noalloc(const float* tiles, float* out_vals, uint16_t* out_states, int64_t n_tiles,
+                                  const uint8_t* lut, int K, int tailbite_ctx, void* stream);
+
+/*
  * Roofline probe (no reference counterpart): launches blocks x threads
  * threads that each issue iters*128 independent __hfma2 instructions.  Time
  * it with events on `stream`: HFMA2 rate = blocks*threads*iters*128 / time.

@@ -32,6 +32,7 @@ EXPORTED = (
     "kq_pack_trellis",
     "kq_unpack_trellis_states",
     "kq_probe_hfma2",
+    "kq_quantize_tiles_sqg_noalloc",
 )
 
 _lib = None
@@ -66,6 +67,7 @@ def load() -> ctypes.CDLL:
         L.kq_pack_trellis.argtypes = [P, I64, I, P, P]
         L.kq_unpack_trellis_states.argtypes = [P, I64, I, P, P]
         L.kq_probe_hfma2.argtypes = [P, I, I, I, P]
+        L.kq_quantize_tiles_sqg_noalloc.argtypes = [P, P, P, I64, P, I, I, P]
         for name in EXPORTED:
             f = getattr(L, name)
             if name not in ("kq_last_error", "kq_viterbi_workspace_bytes") and f.restype is ctypes.c_int:

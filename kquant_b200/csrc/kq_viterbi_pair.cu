@@ -499,4 +499,41 @@ template int pair_launch<3>(const float*, int64_t, const uint16_t*, int, float*,
 template int pair_launch<4>(const float*, int64_t, const uint16_t*, int, float*, uint16_t*, uint8_t*, size_t,
                             cudaStream_t);
 
+// Launch with a grid bounded by a fixed decision buffer: at most
+// dec_bytes / (2 jobs x 256 rows x row bytes) CTAs, each looping over pairs.
+// Serves callers whose scratch is a fixed-size region (kq_noalloc.cu).
+template <int K>
+static int pair_launch_bounded(const float* tiles, int64_t n, const uint16_t* labels, int C, float* vals,
+                               uint16_t* states, uint8_t* dec, size_t dec_bytes, cudaStream_t stream) {
+    int sms = 0;
+    if (int rc = sm_count(&sms)) return rc;
+    const size_t per_cta = (size_t)kJobs * 256 * PairMap<K>::ROW_BYTES;
+    const int64_t pairs = (n + 1) / 2;
+    int64_t grid = (int64_t)(dec_bytes / per_cta);
+    if (grid > sms) grid = sms;
+    if (grid > pairs) grid = pairs;
+    if (grid < 1) {
+        set_error("bounded viterbi: decision buffer of %zu bytes holds no CTA (needs %zu)", dec_bytes, per_cta);
+        return KQ_ERR_WORKSPACE;
+    }
+    const int njobs = pairs > grid ? kJobs : 1;
+    const size_t sm = pair_smem_bytes<K>();
+    cudaError_t e = cudaFuncSetAttribute(pair_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
+    pair_kernel<K><<<(int)grid, kThreads, sm, stream>>>(tiles, n, reinterpret_cast<const uint32_t*>(labels),
+                                                        reinterpret_cast<const __half*>(labels), C, njobs, vals,
+                                                        states, dec);
+    return check_launch("pair_kernel");
+}
+
+int viterbi_encode_bounded(const float* tiles, int64_t n, int K, const uint16_t* labels, int C, float* vals,
+                           uint16_t* states, uint8_t* dec, size_t dec_bytes, cudaStream_t stream) {
+    switch (K) {
+    case 2: return pair_launch_bounded<2>(tiles, n, labels, C, vals, states, dec, dec_bytes, stream);
+    case 3: return pair_launch_bounded<3>(tiles, n, labels, C, vals, states, dec, dec_bytes, stream);
+    case 4: return pair_launch_bounded<4>(tiles, n, labels, C, vals, states, dec, dec_bytes, stream);
+    default: set_error("viterbi: K must be 2, 3 or 4 (got %d)", K); return KQ_ERR_ARG;
+    }
+}
+
 }  // namespace kq
