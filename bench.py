@@ -228,6 +228,31 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_viterbi_case(args, local):
+    """Tile kernel alone on random N(0,1) tiles: the small case used for ncu captures."""
+    from kquant_b200 import _native
+    from kquant_b200.codebooks import sqg_xor_cheb_t12_bytes
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    labels = _native.build_labels(_native.KQ_CB_SQG, sqg_xor_cheb_t12_bytes(args.K).to(device), device)
+    g = torch.Generator(device=device).manual_seed(5)
+    tiles = torch.randn((args.tiles, 256), generator=g, device=device)
+    for _ in range(args.warmup):
+        _native.viterbi_encode(tiles, args.K, labels, CTX)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        _native.viterbi_encode(tiles, args.K, labels, CTX)
+    b.record()
+    torch.cuda.synchronize()
+    sec = a.elapsed_time(b) / 1e3 / max(args.steps, 1)
+    rate = _native.measure_hfma2_rate(device)
+    relax = args.tiles * (2 * CTX + 256) * 65536
+    print(json.dumps({"case": "viterbi", "K": args.K, "tiles": args.tiles, "ms_per_launch": sec * 1e3,
+                      "tiles_per_s": args.tiles / sec, "frac_of_fp16_alu_peak": 3 * relax / sec / (2 * rate)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -236,8 +261,15 @@ def main():
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi"],
+                    help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
+    ap.add_argument("--tiles", type=int, default=1184)
+    ap.add_argument("--K", type=int, default=K_BITS)
     args = ap.parse_args()
     world, rank, local = _dist()
+    if args.case == "viterbi":
+        run_viterbi_case(args, local)
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         return
@@ -285,7 +317,7 @@ def main():
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     es.record()
     d2h = 0
-    for _ in range(args.e2e_steps):
+    for _ in range(max(args.e2e_steps, 0)):
         dw = [w.to(device, non_blocking=True) for w in host_w]
         dh13, dh2 = (h.to(device, non_blocking=True) for h in host_h)
         out = encode_triplet([to_exl(w) for w in dw], dh13, dh2, device)
@@ -294,7 +326,7 @@ def main():
         d2h = sum(v.numel() * v.element_size() for o in host_out for v in o.values()) + proxy_host.numel() * 8
     ee.record()
     torch.cuda.synchronize()
-    e_elapsed = _allreduce_max(es.elapsed_time(ee) / 1e3, world)
+    e_elapsed = max(_allreduce_max(es.elapsed_time(ee) / 1e3, world), 1e-9)
 
     total_weights = weights_per_step() * world
     value = total_weights * args.steps / elapsed / 1e6
