@@ -1,0 +1,62 @@
+"""End-to-end parity of the backend against fixtures made by the reference backend itself.
+
+tests/golden/make_backend_fixtures.py ran the reference's exl3_encoder_backend
+(CPU, C-oracle tile quantizer) on these seeded inputs.  Here the same inputs go
+through kquant_b200 on the GPU, with the sign draws taken from the same CPU
+generator.  Criteria from the north star: proxy error within 1% relative, and,
+where the rotated inputs agree (identical fp16 scales), bit-exact codes and
+reconstruction within 1e-3 max-abs.  A case whose fp32 host maths rounds one
+fp16 scale differently (CPU vs GPU summation order) legitimately diverges in the
+codes downstream of it; it is still held to the proxy criterion.
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from kquant_b200 import exl3_encoder_backend as be
+from kquant_b200.ldlq import make_shared_h
+from tests.golden.backend_cases import CASES, make_inputs
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture
+def cpu_sign_draws(monkeypatch):
+    real = torch.randn
+
+    def randn(*size, device=None, **kw):
+        out = real(*size, **kw)
+        return out.to(device) if device is not None else out
+
+    monkeypatch.setattr(torch, "randn", randn)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_backend_matches_reference_fixture(cuda_device, cpu_sign_draws, name):
+    ref = np.load(GOLDEN / f"backend_{name}.npz")
+    w, h, args = make_inputs(CASES[name], cuda_device)
+    wq, proxy, out = be.quantize_qsrt(w.clone(), make_shared_h(w.shape[0], cuda_device, h), args, True)
+    torch.cuda.synchronize()
+    ref_proxy = float(ref["proxy"])
+    states = be._native.unpack_trellis_states(out["trellis"], args["K"]).cpu().numpy()
+    stats = {
+        "proxy": proxy, "ref_proxy": ref_proxy, "proxy_rel": abs(proxy - ref_proxy) / ref_proxy,
+        "g_scale": args["g_scale"], "ref_g_scale": float(ref["g_scale"]),
+        "suh_equal": float((out["suh"].cpu().numpy() == ref["suh"]).mean()),
+        "svh_equal": float((out["svh"].cpu().numpy() == ref["svh"]).mean()),
+        "states_equal": float((states == ref["states"]).mean()),
+        "recon_maxabs": float(np.abs(wq.cpu().numpy() - ref["weight_q"]).max()),
+        "recon_rel": float(np.linalg.norm(wq.cpu().numpy() - ref["weight_q"]) / np.linalg.norm(ref["weight_q"])),
+    }
+    print(name, json.dumps(stats))
+    assert stats["proxy_rel"] < 0.01
+    assert abs(stats["g_scale"] - stats["ref_g_scale"]) / stats["ref_g_scale"] < 1e-3
+    assert stats["suh_equal"] > 0.99 and stats["svh_equal"] > 0.99
+    if stats["suh_equal"] == 1.0 and stats["svh_equal"] == 1.0:
+        # identical rotated inputs: codes bit-exact and reconstruction within 1e-3
+        assert stats["states_equal"] == 1.0
+        assert stats["recon_maxabs"] < 1e-3
