@@ -171,12 +171,14 @@ def _allreduce_max(x: float, world: int) -> float:
 
 
 def _reduce_proxy(results, world):
-    """Per-step reduce of the per-tensor proxy statistics (sum, max) across ranks."""
-    vals = torch.tensor([[r[0] for r in results]], dtype=torch.float64, device="cuda")
-    if world > 1:
-        import torch.distributed as dist
-        dist.all_reduce(vals, op=dist.ReduceOp.SUM)
-    return vals
+    """Per-step NCCL reduce of the per-tensor proxy statistics; slot = rank * 3 + tensor."""
+    from kquant_b200.sharding import reduce_proxy_stats
+    rank = int(os.environ.get("RANK", "0"))
+    num = torch.zeros(3 * world, dtype=torch.float64, device="cuda")
+    den = torch.zeros(3 * world, dtype=torch.float64, device="cuda")
+    num[3 * rank:3 * rank + 3] = torch.tensor([r[0] for r in results], dtype=torch.float64)
+    den[3 * rank:3 * rank + 3] = 1.0
+    return reduce_proxy_stats(num, den)
 
 
 def cpu_tile_rate(seconds_target: float = 15.0):
