@@ -369,23 +369,60 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
         uint16_t* my_enc = enc + (tb_job * 2 + tb_tile) * 256;
 
         if (F < 0) {
-            // Every active job is in a traceback phase: walk to the phase ends without barriers.
-            if (my_tb) {
-                const int steps = (my_phase == PH_TP) ? C - my_step : 256 - my_step;
-                for (int s = 0; s < steps; ++s) {
-                    int owner, word, sh;
-                    M::locate(tb.node, tb_tile, owner, word, sh);
-                    const unsigned int w = __ldcg(reinterpret_cast<const unsigned int*>(
-                        my_dec + (size_t)tb.row * M::ROW_BYTES + (size_t)owner * M::WORD_BYTES) + word);
-                    const int d = (int)((w >> sh) & (M::Q - 1));
-                    if (my_phase == PH_TF) my_enc[tb.row] = (uint16_t)((d << (16 - K)) | tb.node);
-                    tb.node = (d << M::DSHIFT) | (tb.node >> K);
-                    --tb.row;
+            // Every active job is in a traceback phase and every thread is idle.
+            // The cost buffer holds nothing live (the next forward step of any
+            // job starts from virtual costs), so it stages chunks of decision
+            // rows: all threads copy the next rows of each job with coalesced
+            // 16-byte loads, then the traceback lanes walk them from shared
+            // memory instead of paying one dependent global load per step.
+            int rem0 = 0, rem1 = 0, row0 = 0, row1 = 0;
+            if (phase[0] == PH_TP) { rem0 = C - step[0]; row0 = C - 1 - step[0]; }
+            if (phase[0] == PH_TF) { rem0 = 256 - step[0]; row0 = 255 - step[0]; }
+            if (phase[1] == PH_TP) { rem1 = C - step[1]; row1 = C - 1 - step[1]; }
+            if (phase[1] == PH_TF) { rem1 = 256 - step[1]; row1 = 255 - step[1]; }
+            const int ntb = (rem0 > 0) + (rem1 > 0);
+            const int cap = (2 * M::NODES * 4) / (ntb * M::ROW_BYTES);    // rows per job per chunk
+            uint8_t* stage = reinterpret_cast<uint8_t*>(cost);
+            uint8_t* slot0 = stage;
+            uint8_t* slot1 = stage + (rem0 > 0 ? (size_t)cap * M::ROW_BYTES : 0);
+            while (rem0 > 0 || rem1 > 0) {
+                const int R0 = min(rem0, cap), R1 = min(rem1, cap);
+                // rows [row - R + 1, row] are contiguous in the job's decision area
+                if (R0 > 0) {
+                    const uint4* src = reinterpret_cast<const uint4*>(dec_job(0) + (size_t)(row0 - R0 + 1) * M::ROW_BYTES);
+                    uint4* dst = reinterpret_cast<uint4*>(slot0);
+                    for (int i = tid; i < R0 * M::ROW_BYTES / 16; i += kThreads) dst[i] = __ldcg(src + i);
                 }
-                if (my_phase == PH_TP) {
-                    es_sh[tb_job * 2 + tb_tile] = tb.node;
-                    tb.row = 255;
+                if (R1 > 0) {
+                    const uint4* src = reinterpret_cast<const uint4*>(dec_job(1) + (size_t)(row1 - R1 + 1) * M::ROW_BYTES);
+                    uint4* dst = reinterpret_cast<uint4*>(slot1);
+                    for (int i = tid; i < R1 * M::ROW_BYTES / 16; i += kThreads) dst[i] = __ldcg(src + i);
                 }
+                __syncthreads();
+                if (my_tb) {
+                    const int R = tb_job ? R1 : R0;
+                    const int first = (tb_job ? row1 : row0) - R + 1;
+                    const uint8_t* sl = tb_job ? slot1 : slot0;
+                    for (int s2 = 0; s2 < R; ++s2) {
+                        int owner, word, sh;
+                        M::locate(tb.node, tb_tile, owner, word, sh);
+                        const unsigned int w = reinterpret_cast<const unsigned int*>(
+                            sl + (size_t)(tb.row - first) * M::ROW_BYTES + (size_t)owner * M::WORD_BYTES)[word];
+                        const int d = (int)((w >> sh) & (M::Q - 1));
+                        if (my_phase == PH_TF) my_enc[tb.row] = (uint16_t)((d << (16 - K)) | tb.node);
+                        tb.node = (d << M::DSHIFT) | (tb.node >> K);
+                        --tb.row;
+                    }
+                }
+                __syncthreads();
+                rem0 -= R0;
+                row0 -= R0;
+                rem1 -= R1;
+                row1 -= R1;
+            }
+            if (my_tb && my_phase == PH_TP) {
+                es_sh[tb_job * 2 + tb_tile] = tb.node;
+                tb.row = 255;
             }
             __syncthreads();
 #pragma unroll

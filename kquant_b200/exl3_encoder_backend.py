@@ -278,6 +278,27 @@ def blockwise_preapply_had_r_(x: torch.Tensor, had_dim):
 # --------------------------------------------------------------------------
 
 
+def _host_copy(t: torch.Tensor) -> torch.Tensor:
+    """Stream-ordered copy of a device tensor into pinned host memory.
+
+    The copy completes in stream order; every public entry point of this module
+    reads a proxy scalar back to the host before returning, which orders it.
+    """
+    if not t.is_cuda:
+        return t
+    out = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    out.copy_(t, non_blocking=True)
+    return out
+
+
+def _device_H(H_data: dict, H: torch.Tensor, device) -> torch.Tensor:
+    """The finalised H on ``device``: the resident copy kept by finalize_capture_H, else an upload."""
+    dev_h = H_data.get("_H_device")
+    if dev_h is not None and dev_h.device == torch.device(device):
+        return dev_h
+    return H.to(device)
+
+
 def _is_oom(e: Exception) -> bool:
     return e.__class__.__name__ == "OutOfMemoryError" or "out of memory" in str(e)
 
@@ -312,7 +333,7 @@ def block_ldl(H: torch.Tensor, b: int, quant_args: dict, verbose: bool):
             print(f" !! Out of memory on {H.device}, trying CPU fallback")
             L = torch.linalg.cholesky(H.cpu()).to(H.device)
             break
-    H_cpu = H.cpu()
+    H_cpu = _host_copy(H)
     H.copy_(L)
     del L
     L = H
@@ -323,9 +344,8 @@ def block_ldl(H: torch.Tensor, b: int, quant_args: dict, verbose: bool):
     Lb.copy_(torch.einsum("nmb,mbc->nmc", Lb, DLi))
     L = L.view(n, n)
     blocks = L.view(m, b, m, b)
-    eye = torch.eye(b, device=L.device, dtype=L.dtype)
-    for i in range(m):
-        blocks[i, :, i, :] = eye
+    diag_blocks = torch.arange(m, device=L.device)
+    blocks[diag_blocks, :, diag_blocks, :] = torch.eye(b, device=L.device, dtype=L.dtype)
     return L, H_cpu
 
 
@@ -372,11 +392,15 @@ def finalize_capture_H(H_data: dict, quant_args: dict, verbose: bool):
         if q_fallback:
             L = None
         else:
+            # Keep the rotated, damped H resident for the proxy (B200 has the
+            # room); H_data["H"] still becomes the host copy, as the callers expect.
+            H_data["_H_device"] = H.clone()
             L, H = block_ldl(H, 16, quant_args, verbose)
             idx = torch.arange(k)
             L[idx, idx] = 0
         H_data["L"] = L
-        H = H.cpu()
+        if H.is_cuda:
+            H = _host_copy(H)
         H_data["H"] = H
         H_data["finalized"] = True
         H_data["diag"] = diag
@@ -1215,7 +1239,7 @@ def quantize_qsrt(weight: torch.Tensor, H_data: dict, quant_args: dict, return_w
         H_diag = H_diag.to(device)
     sv = output_signs(n, device, quant_args)
     if H_data["L"] is not None:
-        H_data["L"] = H_data["L"].cpu()
+        H_data["L"] = _host_copy(H_data["L"])
     if L is not None:
         L = L.to(device)
     if swap_to_device is not None:
@@ -1232,7 +1256,7 @@ def quantize_qsrt(weight: torch.Tensor, H_data: dict, quant_args: dict, return_w
             weight_q, encoded_q = ldlq(weight_r, L, quant_args)
         del L
         try:
-            Hd = H.to(device)
+            Hd = _device_H(H_data, H, device)
             num = block_trace(weight_r - weight_q, Hd)
             den = block_trace(weight_r, Hd)
             proxy_err = num / max(den, 1e-8)
@@ -1313,11 +1337,11 @@ def quantize_qsrt_batch(weights: list[torch.Tensor], H_datas: list[dict], quant_
         q_fallback, H, L, su, H_diag = finalize_capture_H(H_data, args, verbose)
         if q_fallback or H is None or L is None:
             raise ValueError("mixed-rate batching requires a non-fallback dense Hessian")
-        H, L, su = H.to(device), L.to(device), su.to(device)
+        H, L, su = _device_H(H_data, H, device), L.to(device), su.to(device)
         if H_diag is not None:
             H_diag = H_diag.to(device)
         if H_data["L"] is not None:
-            H_data["L"] = H_data["L"].cpu()
+            H_data["L"] = _host_copy(H_data["L"])
         sv = output_signs(weight.shape[1], device, args)
         apply_out, weight_r, _, su, sv = regularize(weight, su, sv, args, verbose, H_diag, None, skip_g_scale=True)
         prepared.append({"H": H, "L": L, "weight_r": weight_r, "su": su, "sv": sv, "apply_out_scales": apply_out})
@@ -1472,7 +1496,7 @@ def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], qua
         qa = quant_args_list[t]
         _, su, sv, apply_out = regs[t]
         if Hd is None or not shared_H:
-            Hd = finalized[t][0].to(device)
+            Hd = _device_H(H_datas[t], finalized[t][0], device)
         try:
             num = block_trace(wrs[bi] - wqs[bi], Hd)
             den = block_trace(wrs[bi], Hd)
