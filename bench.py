@@ -274,6 +274,9 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args, world, rank)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
         return
     from kquant_b200 import _native
     device = torch.device("cuda", local)
