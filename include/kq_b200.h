@@ -131,6 +131,19 @@ int kq_quantize_tiles_sqg_noalloc(const float* tiles, float* out_vals, uint16_t*
                                   const uint8_t* lut, int K, int tailbite_ctx, void* stream);
 
 /*
+ * Fused tensor-core GEMM + trace (tcgen05 kind::tf32, TMA-fed):
+ *     *out += sum_{i<M, j<N} (A B^T)[i][j] * D[i][j]
+ * A [M x Kd], B [N x Kd] row-major fp32, D [M x N] with row stride ldd.
+ * M % 128 == 0, N % 256 == 0, Kd % 32 == 0, 16-byte aligned rows.  Inputs
+ * are rounded to TF32 by the tensor cores; accumulation is fp32, the final
+ * reduction fp64.  With A = D = E^T and B = H (symmetric) this is the proxy
+ * numerator tr(E^T H E) of kquant/exl3_encoder_backend.py:1466-1492
+ * (block_trace).  *err is set to 1 if an internal wait timed out.
+ */
+int kq_trace_abt(const float* A, const float* B, const float* D, int64_t M, int64_t N, int64_t Kd, int64_t ldd,
+                 double* out, int* err, void* stream);
+
+/*
  * Roofline probe (no reference counterpart): launches blocks x threads
  * threads that each issue iters*128 independent __hfma2 instructions.  Time
  * it with events on `stream`: HFMA2 rate = blocks*threads*iters*128 / time.

@@ -33,6 +33,7 @@ EXPORTED = (
     "kq_unpack_trellis_states",
     "kq_probe_hfma2",
     "kq_quantize_tiles_sqg_noalloc",
+    "kq_trace_abt",
 )
 
 _lib = None
@@ -68,6 +69,7 @@ def load() -> ctypes.CDLL:
         L.kq_unpack_trellis_states.argtypes = [P, I64, I, P, P]
         L.kq_probe_hfma2.argtypes = [P, I, I, I, P]
         L.kq_quantize_tiles_sqg_noalloc.argtypes = [P, P, P, I64, P, I, I, P]
+        L.kq_trace_abt.argtypes = [P, P, P, I64, I64, I64, I64, P, P, P]
         for name in EXPORTED:
             f = getattr(L, name)
             if name not in ("kq_last_error", "kq_viterbi_workspace_bytes") and f.restype is ctypes.c_int:
@@ -240,3 +242,35 @@ def measure_hfma2_rate(device: torch.device, iters: int = 4096, reps: int = 5) -
             b.synchronize()
             best = min(best, a.elapsed_time(b) / 1e3)
     return blocks * threads * iters * 128 / best
+
+
+def trace_abt_supported(M: int, N: int, Kd: int) -> bool:
+    return M > 0 and N > 0 and Kd > 0 and M % 128 == 0 and N % 256 == 0 and Kd % 32 == 0
+
+
+def trace_abt(A: torch.Tensor, B: torch.Tensor, D: torch.Tensor) -> torch.Tensor:
+    """Device fp64 scalar sum((A @ B.T) * D) on the tensor cores (TF32 inputs, fp32 accumulate)."""
+    for name, t in (("A", A), ("B", B), ("D", D)):
+        _cuda(t, name, torch.float32)
+    M, Kd = A.shape
+    N = B.shape[0]
+    if B.shape[1] != Kd or D.shape != (M, N):
+        raise ValueError("trace_abt: shapes must be A [M, Kd], B [N, Kd], D [M, N]")
+    out = torch.zeros((), dtype=torch.float64, device=A.device)
+    err = torch.zeros((), dtype=torch.int32, device=A.device)
+    with torch.cuda.device(A.device):
+        _check(load().kq_trace_abt(A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, Kd, N, out.data_ptr(),
+                                   err.data_ptr(), _stream(A.device)), "kq_trace_abt")
+    stats.launches += 1
+    _trace_errors.append(err)
+    return out
+
+
+_trace_errors: list = []
+
+
+def check_trace_errors() -> None:
+    """Raise if any tensor-core trace launch reported an internal timeout (one device sync)."""
+    errs, _trace_errors[:] = list(_trace_errors), []
+    if errs and int(torch.stack(errs).sum().item()):
+        raise KQError("kq_trace_abt: an internal wait timed out")

@@ -1,0 +1,252 @@
+// Fused tensor-core GEMM + trace epilogue on sm_100a (tcgen05 + TMA):
+//
+//     out += sum_{i < M, j < N} (A B^T)[i][j] * D[i][j]
+//
+// A [M x Kd] and B [N x Kd] are row-major fp32 (both K-major); D [M x N]
+// has row stride ldd.  The proxy error numerator of the encoder,
+// tr(E^T H E) (kquant/exl3_encoder_backend.py:1466-1492), is this with
+// A = D = E^T and B = H (H symmetric).  No product matrix is ever written:
+// each 128 x 256 tile lives in tensor memory and is reduced in the epilogue.
+//
+// Per CTA (128 threads, one 128 x 256 output tile):
+//  * warp 0, one lane: TMA loads of 128 x 32 (A) and 256 x 32 (B) fp32 tiles,
+//    128-byte swizzle, into a 4-stage shared-memory ring (mbarrier complete_tx);
+//  * warp 1, one lane: tcgen05.mma.cta_group::1.kind::tf32, M=128 N=256 K=8,
+//    four per stage, accumulating in a 256-column TMEM tile; tcgen05.commit
+//    frees each stage and finally signals the epilogue;
+//  * all four warps: tcgen05.ld 32x32b (warp w owns TMEM lanes 32w..32w+31 =
+//    tile rows), multiply by D, reduce in fp64, one atomicAdd per warp.
+// Inputs enter the tensor cores as TF32 (10-bit mantissa), accumulation is
+// fp32.  Every mbarrier wait is bounded: on timeout the kernel sets *err and
+// still releases its tensor memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include "kq_common.cuh"
+
+namespace kq {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 4;           // 16 KiB
+constexpr int B_BYTES = BN * BK * 4;           // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;   // + alignment slack
+constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr uint32_t kTmemCols = 256;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_addr(bar);
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major tile, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), LBO unused (1), descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: D fp32, A and B TF32, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(128, 1)
+trace_abt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 const float* __restrict__ D, int64_t ldd, int M, int N, int Kd, double* __restrict__ out,
+                 int* __restrict__ err)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t done_bar;
+    __shared__ uint32_t tmem_slot;
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = N / BN;
+    const int m0 = (blockIdx.x / n_tiles) * BM;
+    const int n0 = (blockIdx.x % n_tiles) * BN;
+    const int k_iters = Kd / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        mbar_init(&done_bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+
+    if (warp == 0 && lane == 0) {
+        for (int it = 0; it < k_iters && ok; ++it) {
+            const int s = it % STAGES;
+            ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1);
+            if (!ok) break;
+            mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+            uint8_t* sa = smem + s * STAGE_BYTES;
+            tma_load_2d(sa, &map_a, it * BK, m0, &full_bar[s]);
+            tma_load_2d(sa + A_BYTES, &map_b, it * BK, n0, &full_bar[s]);
+        }
+        if (!ok) atomicExch(err, 1);
+    } else if (warp == 1 && lane == 0) {
+        for (int it = 0; it < k_iters && ok; ++it) {
+            const int s = it % STAGES;
+            ok = mbar_wait(&full_bar[s], (it / STAGES) & 1);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a = smem_addr(smem + s * STAGE_BYTES);
+            const uint64_t ad = smem_desc(a), bd = smem_desc(a + A_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk)       // K = 8 tf32 = 32 bytes = +2 in the 16-byte address field
+                mma_tf32(tmem, ad + 2 * kk, bd + 2 * kk, (it | kk) != 0);
+            mma_commit(&empty_bar[s]);
+        }
+        if (ok) mma_commit(&done_bar);
+        else atomicExch(err, 1);
+    }
+    __syncwarp();
+
+    // Epilogue: all four warps, warp w reads accumulator rows 32w..32w+31.
+    const bool ready = mbar_wait(&done_bar, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    double acc = 0.0;
+    const bool go = __all_sync(0xFFFFFFFFu, ready && !*reinterpret_cast<volatile int*>(err));
+    if (go) {
+        const int row = m0 + warp * 32 + lane;
+        const float* drow = D + (int64_t)row * ldd + n0;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+            uint32_t v[16];
+            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            float part = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 d = *reinterpret_cast<const float4*>(drow + c0 + 4 * q);
+                part += __uint_as_float(v[4 * q]) * d.x + __uint_as_float(v[4 * q + 1]) * d.y +
+                        __uint_as_float(v[4 * q + 2]) * d.z + __uint_as_float(v[4 * q + 3]) * d.w;
+            }
+            acc += (double)part;
+        }
+    } else if (threadIdx.x == 0) {
+        atomicExch(err, 1);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_down_sync(0xFFFFFFFFu, acc, off);
+    if (lane == 0 && acc != 0.0) atomicAdd(out, acc);
+
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+int make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) { set_error("cuTensorMapEncodeTiled unavailable"); return KQ_ERR_CUDA; }
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) { set_error("cuTensorMapEncodeTiled failed (%d)", (int)r); return KQ_ERR_CUDA; }
+    return KQ_OK;
+}
+
+}  // namespace
+}  // namespace kq
+
+extern "C" int kq_trace_abt(const float* A, const float* B, const float* D, int64_t M, int64_t N, int64_t Kd,
+                            int64_t ldd, double* out, int* err, void* stream) {
+    using namespace kq;
+    if (!A || !B || !D || !out || !err) { set_error("kq_trace_abt: null pointer"); return KQ_ERR_ARG; }
+    if (M <= 0 || N <= 0 || Kd <= 0 || M % BM || N % BN || Kd % BK || ldd < N || ldd % 4) {
+        set_error("kq_trace_abt: need M %% 128 == 0, N %% 256 == 0, Kd %% 32 == 0, ldd >= N, ldd %% 4 == 0 "
+                  "(got M=%lld N=%lld Kd=%lld ldd=%lld)", (long long)M, (long long)N, (long long)Kd, (long long)ldd);
+        return KQ_ERR_ARG;
+    }
+    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)D) & 15) { set_error("kq_trace_abt: 16-byte alignment"); return KQ_ERR_ALIGN; }
+    if ((M / BM) * (N / BN) > 0x7FFFFFFF || M > 0x7FFFFFFF || N > 0x7FFFFFFF || Kd > 0x7FFFFFFF) {
+        set_error("kq_trace_abt: problem too large");
+        return KQ_ERR_ARG;
+    }
+    CUtensorMap ma, mb;
+    if (int rc = make_map(&ma, A, M, Kd, BM)) return rc;
+    if (int rc = make_map(&mb, B, N, Kd, BN)) return rc;
+    cudaError_t e = cudaFuncSetAttribute(trace_abt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
+    const int grid = (int)((M / BM) * (N / BN));
+    trace_abt_kernel<<<grid, 128, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, D, ldd, (int)M, (int)N,
+                                                                                   (int)Kd, out, err);
+    return check_launch("trace_abt_kernel");
+}

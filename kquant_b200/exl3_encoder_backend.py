@@ -939,12 +939,29 @@ def fallback_quant(weight: torch.Tensor, q_device, quant_args: dict, pb=None):
 # --------------------------------------------------------------------------
 
 
+# The proxy traces run as one fused tcgen05 GEMM + trace kernel (TF32 operands,
+# fp32 accumulation, fp64 reduction) when the shapes tile; the proxy is a
+# 1%-tolerance measurement, so TF32 operands are within its contract.
+PROXY_ON_TENSOR_CORES = True
+
+
 def block_trace_parts(A, B, block_size=1024):
-    """Column-block terms of trace(A^T B A), on device (kquant/exl3_encoder_backend.py:1466-1479)."""
+    """Device terms of trace(A^T B A) (kquant/exl3_encoder_backend.py:1466-1479).
+
+    On the tensor-core path the result is a single term:
+    trace(A^T B A) = sum((A^T B) * A^T), computed by kq_trace_abt with
+    operands A^T [n, k] and B^T [k, k] (no symmetry of B assumed).  Otherwise
+    the column blocks of B are reduced with cuBLAS FP32.
+    """
+    k, n = A.shape
+    if (PROXY_ON_TENSOR_CORES and A.is_cuda and B.is_cuda and A.dtype == torch.float32 and B.dtype == torch.float32
+            and B.shape == (k, k) and _native.trace_abt_supported(n, k, k)):
+        At = A.T.contiguous()
+        return _native.trace_abt(At, B.T.contiguous(), At).reshape(1)
     parts = []
     for j in range(0, B.shape[1], block_size):
-        k = min(j + block_size, B.shape[1])
-        parts.append(torch.sum((A.T @ B[:, j:k]) * A[j:k, :].T))
+        e = min(j + block_size, B.shape[1])
+        parts.append(torch.sum((A.T @ B[:, j:e]) * A[j:e, :].T))
     return torch.stack(parts)
 
 
@@ -953,6 +970,7 @@ def block_trace(A, B, block_size=1024):
     total = 0.0
     for p in block_trace_parts(A, B, block_size).cpu():
         total += p.item()
+    _native.check_trace_errors()
     return total
 
 
@@ -1288,7 +1306,9 @@ def _trace_rows(parts: list[torch.Tensor]) -> list[float]:
     """Sum each row of block-trace terms on the host, in order, in fp64."""
     if not parts:
         return []
-    rows = torch.stack(parts).cpu()
+    width = max(p.numel() for p in parts)
+    rows = torch.stack([torch.nn.functional.pad(p.double(), (0, width - p.numel())) for p in parts]).cpu()
+    _native.check_trace_errors()
     values = []
     for row in rows:
         total = 0.0
