@@ -255,6 +255,31 @@ def run_viterbi_case(args, local):
                       "tiles_per_s": args.tiles / sec, "frac_of_fp16_alu_peak": 3 * relax / sec / (2 * rate)}))
 
 
+def run_trace_case(args, local):
+    """Proxy numerator tr(E^T H E) of the gate/up encode (k=7168, n=4096) on the tcgen05 trace kernel."""
+    from kquant_b200 import _native
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    k, n = HIDDEN, 2 * INTER
+    g = torch.Generator(device=device).manual_seed(9)
+    H = torch.randn((k, k), generator=g, device=device)
+    Et = torch.randn((n, k), generator=g, device=device)
+    for _ in range(args.warmup):
+        _native.trace_abt(Et, H, Et)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        _native.trace_abt(Et, H, Et)
+    b.record()
+    torch.cuda.synchronize()
+    _native.check_trace_errors()
+    sec = a.elapsed_time(b) / 1e3 / max(args.steps, 1)
+    flops = 2.0 * n * k * k
+    print(json.dumps({"case": "trace", "M": n, "N": k, "Kd": k, "ms_per_launch": sec * 1e3,
+                      "tflops": flops / sec / 1e12, "algorithmic_bytes": 4 * (k * k + 2 * n * k)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -263,7 +288,7 @@ def main():
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi"],
+    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
@@ -271,6 +296,9 @@ def main():
     world, rank, local = _dist()
     if args.case == "viterbi":
         run_viterbi_case(args, local)
+        return
+    if args.case == "trace":
+        run_trace_case(args, local)
         return
     if args.impl == "reference":
         run_reference(args, world, rank)
