@@ -280,6 +280,45 @@ def run_trace_case(args, local):
                       "tflops": flops / sec / 1e12, "algorithmic_bytes": 4 * (k * k + 2 * n * k)}))
 
 
+def _hbm_peak():
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+def _time(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / 1e3 / max(steps, 1)
+
+
+def run_pack_case(args, local):
+    """Trellis pack / unpack+closure over the triplet's tiles (HBM-bound rows P and S)."""
+    from kquant_b200 import _native
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    n = weights_per_step() // 256
+    K = args.K
+    states = torch.randint(-32768, 32767, (n, 256), dtype=torch.int16, device=device)
+    packed = _native.pack_trellis(states, K)
+    peak, src = _hbm_peak()
+    out = {"case": "pack", "K": K, "tiles": n, "hbm_peak_gbs": peak, "peak_source": src}
+    t = _time(lambda: _native.pack_trellis(states, K), args.steps, args.warmup)
+    byt = n * (512 + 32 * K)
+    out.update(pack_ms=t * 1e3, pack_gbs=byt / t / 1e9, pack_frac=byt / t / 1e9 / peak)
+    t = _time(lambda: _native.unpack_trellis_states(packed, K), args.steps, args.warmup)
+    out.update(unpack_ms=t * 1e3, unpack_gbs=byt / t / 1e9, unpack_frac=byt / t / 1e9 / peak)
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -288,7 +327,7 @@ def main():
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace"],
+    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace", "pack"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
@@ -299,6 +338,9 @@ def main():
         return
     if args.case == "trace":
         run_trace_case(args, local)
+        return
+    if args.case == "pack":
+        run_pack_case(args, local)
         return
     if args.impl == "reference":
         run_reference(args, world, rank)
