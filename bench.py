@@ -103,7 +103,9 @@ def encode_triplet(weights_exl, h13, h2, device):
 
 
 def to_exl(w_hf: torch.Tensor) -> torch.Tensor:
-    return w_hf.float().T.contiguous()
+    """bf16 HF [out, in] -> fp32 EXL [in, out] on the transposing load kernel."""
+    from kquant_b200 import _native
+    return _native.bf16_to_f32_transposed(w_hf)
 
 
 class ClockSampler:
@@ -319,6 +321,26 @@ def run_pack_case(args, local):
     print(json.dumps(out))
 
 
+def run_load_case(args, local):
+    """bf16 HF -> fp32 EXL weight load of the triplet (gate, up, down), plain and with a row gather."""
+    from kquant_b200 import _native
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(3)
+    ws = [torch.randn(s, generator=g, device=device).to(torch.bfloat16)
+          for s in ((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER))]
+    perms = [torch.randperm(w.shape[0], generator=g, device=device) for w in ws]
+    peak, src = _hbm_peak()
+    byt = sum(w.numel() for w in ws) * (2 + 4)
+    t = _time(lambda: [_native.bf16_to_f32_transposed(w) for w in ws], args.steps, args.warmup)
+    tp = _time(lambda: [_native.bf16_to_f32_transposed(w, p) for w, p in zip(ws, perms)], args.steps, args.warmup)
+    tt = _time(lambda: [w.float().T.contiguous() for w in ws], args.steps, args.warmup)
+    print(json.dumps({"case": "load", "weights": sum(w.numel() for w in ws), "bytes": byt, "hbm_peak_gbs": peak,
+                      "peak_source": src, "ms": t * 1e3, "gbs": byt / t / 1e9, "frac": byt / t / 1e9 / peak,
+                      "gather_ms": tp * 1e3, "gather_gbs": byt / tp / 1e9,
+                      "torch_float_T_contiguous_ms": tt * 1e3}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -327,7 +349,7 @@ def main():
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace", "pack"],
+    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace", "pack", "load"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
@@ -341,6 +363,9 @@ def main():
         return
     if args.case == "pack":
         run_pack_case(args, local)
+        return
+    if args.case == "load":
+        run_load_case(args, local)
         return
     if args.impl == "reference":
         run_reference(args, world, rank)

@@ -144,6 +144,16 @@ int kq_trace_abt(const float* A, const float* B, const float* D, int64_t M, int6
                  double* out, int* err, void* stream);
 
 /*
+ * Weight load: bf16 [rows x cols] (row stride ld_src elements; HF [out, in])
+ * -> fp32 [cols x rows] (EXL [in, out]), dst[c][r] = src[row_perm[r]][c]
+ * (row_perm may be NULL).  Replaces the caller-side
+ * source.index_select(0, perm).T.contiguous() of
+ * kquant/pack/qsrt_encoder.py:554-569 (_encoder_weight) for bf16 sources.
+ */
+int kq_bf16_to_f32_transposed(const uint16_t* src, int64_t rows, int64_t cols, int64_t ld_src,
+                              const int64_t* row_perm, float* dst, void* stream);
+
+/*
  * Roofline probe (no reference counterpart): launches blocks x threads
  * threads that each issue iters*128 independent __hfma2 instructions.  Time
  * it with events on `stream`: HFMA2 rate = blocks*threads*iters*128 / time.

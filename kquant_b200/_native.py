@@ -34,6 +34,7 @@ EXPORTED = (
     "kq_probe_hfma2",
     "kq_quantize_tiles_sqg_noalloc",
     "kq_trace_abt",
+    "kq_bf16_to_f32_transposed",
 )
 
 _lib = None
@@ -70,6 +71,7 @@ def load() -> ctypes.CDLL:
         L.kq_probe_hfma2.argtypes = [P, I, I, I, P]
         L.kq_quantize_tiles_sqg_noalloc.argtypes = [P, P, P, I64, P, I, I, P]
         L.kq_trace_abt.argtypes = [P, P, P, I64, I64, I64, I64, P, P, P]
+        L.kq_bf16_to_f32_transposed.argtypes = [P, I64, I64, I64, P, P, P]
         for name in EXPORTED:
             f = getattr(L, name)
             if name not in ("kq_last_error", "kq_viterbi_workspace_bytes") and f.restype is ctypes.c_int:
@@ -274,3 +276,21 @@ def check_trace_errors() -> None:
     errs, _trace_errors[:] = list(_trace_errors), []
     if errs and int(torch.stack(errs).sum().item()):
         raise KQError("kq_trace_abt: an internal wait timed out")
+
+
+def bf16_to_f32_transposed(src: torch.Tensor, row_perm: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [rows, cols] -> fp32 [cols, rows] with optional row gather: out[c, r] = src[row_perm[r], c]."""
+    if not src.is_cuda or src.dtype != torch.bfloat16 or src.ndim != 2 or src.stride(1) != 1:
+        raise ValueError("src must be a CUDA bf16 matrix with unit column stride")
+    rows = src.shape[0] if row_perm is None else row_perm.shape[0]
+    cols = src.shape[1]
+    pp = None
+    if row_perm is not None:
+        _cuda(row_perm, "row_perm", torch.int64)
+        pp = row_perm.data_ptr()
+    out = torch.empty((cols, rows), dtype=torch.float32, device=src.device)
+    with torch.cuda.device(src.device):
+        _check(load().kq_bf16_to_f32_transposed(src.data_ptr(), rows, cols, src.stride(0), pp, out.data_ptr(),
+                                                _stream(src.device)), "kq_bf16_to_f32_transposed")
+    stats.launches += 1
+    return out

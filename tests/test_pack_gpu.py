@@ -44,3 +44,13 @@ def test_pack_empty_and_large(native, cuda_device):
     packed = native.pack_trellis(big, 3)
     edges = native.unpack_trellis_states(packed, 3) & 7
     assert torch.equal(edges, big & 7)
+
+
+@pytest.mark.parametrize("rows,cols,perm", [(2048, 7168, False), (7168, 2048, True), (100, 136, True), (64, 8, False)])
+def test_bf16_transposed_load(native, cuda_device, rows, cols, perm):
+    g = torch.Generator(device=cuda_device).manual_seed(rows + cols)
+    src = torch.randn((rows, cols), generator=g, device=cuda_device).to(torch.bfloat16)
+    p = torch.randperm(rows, generator=g, device=cuda_device) if perm else None
+    got = native.bf16_to_f32_transposed(src, p)
+    ref = (src.index_select(0, p) if perm else src).float().T.contiguous()
+    assert torch.equal(got, ref)
