@@ -341,6 +341,27 @@ def run_load_case(args, local):
                       "torch_float_T_contiguous_ms": tt * 1e3}))
 
 
+def run_hessian_case(args, local):
+    """H13 accumulation from 8192 tokens of hidden 7168 (the encoder's input Hessian) on the tensor cores."""
+    from kquant_b200.capture import accumulate_hessian
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(4)
+    x = torch.randn((TOKENS, HIDDEN), generator=g, device=device)
+    w = torch.rand(TOKENS, generator=g, device=device) + 0.5
+    flops = 2.0 * TOKENS * HIDDEN * HIDDEN
+    out = {"case": "hessian", "tokens": TOKENS, "dim": HIDDEN}
+    for prec in ("tf32", "3xtf32"):
+        t = _time(lambda: accumulate_hessian(x, w, device=device, chunk_rows=TOKENS, precision=prec),
+                  args.steps, args.warmup)
+        out[f"{prec}_ms"] = t * 1e3
+        out[f"{prec}_tflops_effective"] = flops / t / 1e12
+    acc = torch.zeros((HIDDEN, HIDDEN), device=device)
+    t = _time(lambda: acc.addmm_(x.T, x * w.unsqueeze(1)), args.steps, args.warmup)
+    out["torch_fp32_addmm_ms"] = t * 1e3
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -349,7 +370,7 @@ def main():
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace", "pack", "load"],
+    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace", "pack", "load", "hessian"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
@@ -366,6 +387,9 @@ def main():
         return
     if args.case == "load":
         run_load_case(args, local)
+        return
+    if args.case == "hessian":
+        run_hessian_case(args, local)
         return
     if args.impl == "reference":
         run_reference(args, world, rank)

@@ -144,6 +144,17 @@ int kq_trace_abt(const float* A, const float* B, const float* D, int64_t M, int6
                  double* out, int* err, void* stream);
 
 /*
+ * C = alpha * A B^T + beta * C on the tensor cores (tcgen05 kind::tf32, TMA
+ * fed, TMEM accumulator).  Same shape rules as kq_trace_abt; C [M x N] with
+ * row stride ldc.  Used for the Hessian accumulation sum_t w_t x_t x_t^T that
+ * kquant/capture.py:713-730 (_accumulate_hessian) performs with FP32 addmm;
+ * callers wanting FP32-grade accuracy issue three calls on TF32 hi/lo
+ * splits (hi*hi + hi*lo + lo*hi).
+ */
+int kq_gemm_abt_tf32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t Kd, int64_t ldc,
+                     float alpha, float beta, int* err, void* stream);
+
+/*
  * Weight load: bf16 [rows x cols] (row stride ld_src elements; HF [out, in])
  * -> fp32 [cols x rows] (EXL [in, out]), dst[c][r] = src[row_perm[r]][c]
  * (row_perm may be NULL).  Replaces the caller-side

@@ -35,6 +35,7 @@ EXPORTED = (
     "kq_quantize_tiles_sqg_noalloc",
     "kq_trace_abt",
     "kq_bf16_to_f32_transposed",
+    "kq_gemm_abt_tf32",
 )
 
 _lib = None
@@ -72,6 +73,7 @@ def load() -> ctypes.CDLL:
         L.kq_quantize_tiles_sqg_noalloc.argtypes = [P, P, P, I64, P, I, I, P]
         L.kq_trace_abt.argtypes = [P, P, P, I64, I64, I64, I64, P, P, P]
         L.kq_bf16_to_f32_transposed.argtypes = [P, I64, I64, I64, P, P, P]
+        L.kq_gemm_abt_tf32.argtypes = [P, P, P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_float, P, P]
         for name in EXPORTED:
             f = getattr(L, name)
             if name not in ("kq_last_error", "kq_viterbi_workspace_bytes") and f.restype is ctypes.c_int:
@@ -294,3 +296,19 @@ def bf16_to_f32_transposed(src: torch.Tensor, row_perm: torch.Tensor | None = No
                                                 _stream(src.device)), "kq_bf16_to_f32_transposed")
     stats.launches += 1
     return out
+
+
+def gemm_abt_tf32(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, alpha: float = 1.0, beta: float = 1.0) -> None:
+    """C = alpha * A @ B.T + beta * C on the tensor cores (TF32 operands), in place."""
+    for name, t in (("A", A), ("B", B), ("C", C)):
+        _cuda(t, name, torch.float32)
+    M, Kd = A.shape
+    N = B.shape[0]
+    if B.shape[1] != Kd or C.shape != (M, N):
+        raise ValueError("gemm_abt_tf32: shapes must be A [M, Kd], B [N, Kd], C [M, N]")
+    err = torch.zeros((), dtype=torch.int32, device=A.device)
+    with torch.cuda.device(A.device):
+        _check(load().kq_gemm_abt_tf32(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, Kd, N, float(alpha),
+                                       float(beta), err.data_ptr(), _stream(A.device)), "kq_gemm_abt_tf32")
+    stats.launches += 1
+    _trace_errors.append(err)

@@ -1,6 +1,7 @@
-// Fused tensor-core GEMM + trace epilogue on sm_100a (tcgen05 + TMA):
+// Tensor-core GEMMs on sm_100a (tcgen05 + TMA) with two epilogues:
 //
-//     out += sum_{i < M, j < N} (A B^T)[i][j] * D[i][j]
+//     trace:  out += sum_{i < M, j < N} (A B^T)[i][j] * D[i][j]
+//     store:  D = alpha * A B^T + beta * D
 //
 // A [M x Kd] and B [N x Kd] are row-major fp32 (both K-major); D [M x N]
 // has row stride ldd.  The proxy error numerator of the encoder,
@@ -91,10 +92,11 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+// *out += sum (A B^T) * D.
 __global__ void __launch_bounds__(128, 1)
-trace_abt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 const float* __restrict__ D, int64_t ldd, int M, int N, int Kd, double* __restrict__ out,
-                 int* __restrict__ err)
+abt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+           const float* __restrict__ D, int64_t ldd, int M, int N, int Kd, double* __restrict__ out,
+           int* __restrict__ err)
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_bar[STAGES];
@@ -174,14 +176,16 @@ trace_abt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                   "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
                 : "r"(taddr));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            float part = 0.f;
+            {
+                float part = 0.f;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float4 d = *reinterpret_cast<const float4*>(drow + c0 + 4 * q);
-                part += __uint_as_float(v[4 * q]) * d.x + __uint_as_float(v[4 * q + 1]) * d.y +
-                        __uint_as_float(v[4 * q + 2]) * d.z + __uint_as_float(v[4 * q + 3]) * d.w;
+                for (int q = 0; q < 4; ++q) {
+                    const float4 d = *reinterpret_cast<const float4*>(drow + c0 + 4 * q);
+                    part += __uint_as_float(v[4 * q]) * d.x + __uint_as_float(v[4 * q + 1]) * d.y +
+                            __uint_as_float(v[4 * q + 2]) * d.z + __uint_as_float(v[4 * q + 3]) * d.w;
+                }
+                acc += (double)part;
             }
-            acc += (double)part;
         }
     } else if (threadIdx.x == 0) {
         atomicExch(err, 1);
@@ -194,6 +198,158 @@ trace_abt_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// Store GEMM with a drained accumulator: D = alpha * A B^T + beta * D.
+//
+// The tensor-core accumulator is not an IEEE round-to-nearest fp32 adder;
+// over thousands of K steps its error grows to ~1e-5 of the result.  This
+// kernel therefore accumulates only SEG_ITERS k-iterations (128 K values)
+// in tensor memory, and the epilogue warps fold each such partial product
+// into fp32 registers (round-to-nearest adds), so the result carries the
+// accuracy of an fp32 CUDA-core GEMM once the operands are exact in TF32
+// (the 3xTF32 split).  Two 256-column TMEM buffers (all 512 columns)
+// alternate: the MMA warp fills one while the epilogue drains the other.
+//
+// 320 threads: warps 0..7 drain (warp w: TMEM lanes 32*(w%4).., columns
+// 128*(w/4)..+127, 128 running sums per thread), warp 8 lane 0 issues TMA,
+// warp 9 lane 0 issues tcgen05.mma.  All waits are bounded.
+constexpr int SEG_ITERS = 4;
+constexpr int SEG_THREADS = 320;
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__global__ void __launch_bounds__(SEG_THREADS, 1)
+abt_seg_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               float* __restrict__ D, int64_t ldd, int N, int Kd, int* __restrict__ err, float alpha, float beta)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t full_bar[STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[STAGES];
+    __shared__ __align__(8) uint64_t seg_full[2];
+    __shared__ __align__(8) uint64_t seg_empty[2];
+    __shared__ uint32_t tmem_slot;
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = N / BN;
+    const int m0 = (blockIdx.x / n_tiles) * BM;
+    const int n0 = (blockIdx.x % n_tiles) * BN;
+    const int k_iters = Kd / BK;
+    const int n_segs = (k_iters + SEG_ITERS - 1) / SEG_ITERS;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&seg_full[b], 1);
+            mbar_init(&seg_empty[b], 8);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 8) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(2 * kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int it = 0; it < k_iters; ++it) {
+                const int s = it % STAGES;
+                if (!(ok = mbar_wait(&empty_bar[s], ((it / STAGES) & 1) ^ 1))) break;
+                mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+                uint8_t* sa = smem + s * STAGE_BYTES;
+                tma_load_2d(sa, &map_a, it * BK, m0, &full_bar[s]);
+                tma_load_2d(sa + A_BYTES, &map_b, it * BK, n0, &full_bar[s]);
+            }
+            if (!ok) atomicExch(err, 1);
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int seg = 0; seg < n_segs && ok; ++seg) {
+                const int b = seg & 1;
+                if (!(ok = mbar_wait(&seg_empty[b], ((seg >> 1) & 1) ^ 1))) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t acc = tmem + (uint32_t)(b * kTmemCols);
+                const int it_end = min(k_iters, (seg + 1) * SEG_ITERS);
+                for (int it = seg * SEG_ITERS; it < it_end; ++it) {
+                    const int s = it % STAGES;
+                    if (!(ok = mbar_wait(&full_bar[s], (it / STAGES) & 1))) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a = smem_addr(smem + s * STAGE_BYTES);
+                    const uint64_t ad = smem_desc(a), bd = smem_desc(a + A_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk)
+                        mma_tf32(acc, ad + 2 * kk, bd + 2 * kk, (it != seg * SEG_ITERS || kk != 0) ? 1u : 0u);
+                    mma_commit(&empty_bar[s]);
+                }
+                if (ok) mma_commit(&seg_full[b]);
+            }
+            if (!ok) atomicExch(err, 1);
+        }
+    } else {
+        // Drain warps.
+        const int q = warp & 3, h = warp >> 2;
+        float r[BN / 2];
+#pragma unroll
+        for (int i = 0; i < BN / 2; ++i) r[i] = 0.f;
+        bool ok = true;
+        for (int seg = 0; seg < n_segs; ++seg) {
+            const int b = seg & 1;
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(&seg_full[b], (seg >> 1) & 1));
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kTmemCols + h * (BN / 2));
+#pragma unroll
+            for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+                uint32_t v[16];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                    : "r"(base + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int i = 0; i < 16; ++i) r[c0 + i] += __uint_as_float(v[i]);
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&seg_empty[b]);
+        }
+        if (ok && !*reinterpret_cast<volatile int*>(err)) {
+            float* drow = D + (int64_t)(m0 + q * 32 + lane) * ldd + n0 + h * (BN / 2);
+#pragma unroll
+            for (int c = 0; c < BN / 2; c += 4) {
+                float4* dp = reinterpret_cast<float4*>(drow + c);
+                float4 d = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (beta != 0.f) d = *dp;
+                d.x = alpha * r[c] + beta * d.x;
+                d.y = alpha * r[c + 1] + beta * d.y;
+                d.z = alpha * r[c + 2] + beta * d.z;
+                d.w = alpha * r[c + 3] + beta * d.w;
+                *dp = d;
+            }
+        } else if (lane == 0) {
+            atomicExch(err, 1);
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 8) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTmemCols));
     }
 }
 
@@ -226,27 +382,53 @@ int make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t cols, in
 }  // namespace
 }  // namespace kq
 
-extern "C" int kq_trace_abt(const float* A, const float* B, const float* D, int64_t M, int64_t N, int64_t Kd,
-                            int64_t ldd, double* out, int* err, void* stream) {
-    using namespace kq;
-    if (!A || !B || !D || !out || !err) { set_error("kq_trace_abt: null pointer"); return KQ_ERR_ARG; }
+namespace kq {
+namespace {
+
+template <bool STORE>
+int launch_abt(const float* A, const float* B, float* D, int64_t M, int64_t N, int64_t Kd, int64_t ldd, double* out,
+               int* err, float alpha, float beta, void* stream, const char* what) {
+    if (!A || !B || !D || !err || (!STORE && !out)) { set_error("%s: null pointer", what); return KQ_ERR_ARG; }
     if (M <= 0 || N <= 0 || Kd <= 0 || M % BM || N % BN || Kd % BK || ldd < N || ldd % 4) {
-        set_error("kq_trace_abt: need M %% 128 == 0, N %% 256 == 0, Kd %% 32 == 0, ldd >= N, ldd %% 4 == 0 "
-                  "(got M=%lld N=%lld Kd=%lld ldd=%lld)", (long long)M, (long long)N, (long long)Kd, (long long)ldd);
+        set_error("%s: need M %% 128 == 0, N %% 256 == 0, Kd %% 32 == 0, ldd >= N, ldd %% 4 == 0 "
+                  "(got M=%lld N=%lld Kd=%lld ldd=%lld)", what, (long long)M, (long long)N, (long long)Kd,
+                  (long long)ldd);
         return KQ_ERR_ARG;
     }
-    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)D) & 15) { set_error("kq_trace_abt: 16-byte alignment"); return KQ_ERR_ALIGN; }
+    if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)D) & 15) { set_error("%s: 16-byte alignment", what); return KQ_ERR_ALIGN; }
     if ((M / BM) * (N / BN) > 0x7FFFFFFF || M > 0x7FFFFFFF || N > 0x7FFFFFFF || Kd > 0x7FFFFFFF) {
-        set_error("kq_trace_abt: problem too large");
+        set_error("%s: problem too large", what);
         return KQ_ERR_ARG;
     }
     CUtensorMap ma, mb;
     if (int rc = make_map(&ma, A, M, Kd, BM)) return rc;
     if (int rc = make_map(&mb, B, N, Kd, BN)) return rc;
-    cudaError_t e = cudaFuncSetAttribute(trace_abt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
     const int grid = (int)((M / BM) * (N / BN));
-    trace_abt_kernel<<<grid, 128, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, D, ldd, (int)M, (int)N,
-                                                                                   (int)Kd, out, err);
-    return check_launch("trace_abt_kernel");
+    cudaError_t e;
+    if constexpr (STORE) {
+        e = cudaFuncSetAttribute(abt_seg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
+        abt_seg_kernel<<<grid, SEG_THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+            ma, mb, D, ldd, (int)N, (int)Kd, err, alpha, beta);
+    } else {
+        e = cudaFuncSetAttribute(abt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
+        abt_kernel<<<grid, 128, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+            ma, mb, D, ldd, (int)M, (int)N, (int)Kd, out, err);
+    }
+    return check_launch(what);
+}
+
+}  // namespace
+}  // namespace kq
+
+extern "C" int kq_trace_abt(const float* A, const float* B, const float* D, int64_t M, int64_t N, int64_t Kd,
+                            int64_t ldd, double* out, int* err, void* stream) {
+    return kq::launch_abt<false>(A, B, const_cast<float*>(D), M, N, Kd, ldd, out, err, 1.f, 0.f, stream,
+                                 "kq_trace_abt");
+}
+
+extern "C" int kq_gemm_abt_tf32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t Kd,
+                                int64_t ldc, float alpha, float beta, int* err, void* stream) {
+    return kq::launch_abt<true>(A, B, C, M, N, Kd, ldc, nullptr, err, alpha, beta, stream, "kq_gemm_abt_tf32");
 }
