@@ -289,6 +289,13 @@ def _hbm_peak():
         return 6650.0, "fallback"
 
 
+def _peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        return {}
+
+
 def _time(fn, steps, warmup):
     for _ in range(warmup):
         fn()
@@ -342,23 +349,41 @@ def run_load_case(args, local):
 
 
 def run_hessian_case(args, local):
-    """H13 accumulation from 8192 tokens of hidden 7168 (the encoder's input Hessian) on the tensor cores."""
+    """Hessian accumulation (kquant/capture.py:713-730) of --tokens samples of width --dim on the tensor cores.
+
+    Reports the whole call (operand kernel + GEMM), the GEMM launch alone timed with CUDA events on its
+    stream, the tensor work it performs (upper-triangle tiles only; 3 products for 3xTF32) against the
+    TF32 peak (half the measured bf16 figure), and torch's FP32 addmm of the reference on the same data.
+    """
+    from kquant_b200 import _native
     from kquant_b200.capture import accumulate_hessian
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    T, d = args.tokens, args.dim
     g = torch.Generator(device=device).manual_seed(4)
-    x = torch.randn((TOKENS, HIDDEN), generator=g, device=device)
-    w = torch.rand(TOKENS, generator=g, device=device) + 0.5
-    flops = 2.0 * TOKENS * HIDDEN * HIDDEN
-    out = {"case": "hessian", "tokens": TOKENS, "dim": HIDDEN}
-    for prec in ("tf32", "3xtf32"):
-        t = _time(lambda: accumulate_hessian(x, w, device=device, chunk_rows=TOKENS, precision=prec),
+    x = torch.randn((T, d), generator=g, device=device)
+    w = torch.rand(T, generator=g, device=device) + 0.5
+    H = torch.zeros((d, d), device=device)
+    dpad = -(-d // 256) * 256
+    nt = dpad // 256
+    tile_frac = nt * (nt + 1) * 128 * 256 / (dpad * dpad)
+    peak = _peaks().get("bf16_tflops", 1590.0) / 2
+    out = {"case": "hessian", "tokens": T, "dim": d, "tf32_peak_tflops": peak,
+           "upper_tile_fraction": round(tile_frac, 4)}
+    for prec, split in (("tf32", 1), ("3xtf32", 3)):
+        t = _time(lambda: accumulate_hessian(x, w, device=device, chunk_rows=T, precision=prec),
                   args.steps, args.warmup)
-        out[f"{prec}_ms"] = t * 1e3
-        out[f"{prec}_tflops_effective"] = flops / t / 1e12
-    acc = torch.zeros((HIDDEN, HIDDEN), device=device)
+        ws = _native.accumulate_hessian(x, w, H, split)
+        t_all = _time(lambda: _native.accumulate_hessian(x, w, H, split, ws), args.steps, args.warmup)
+        performed = 2.0 * T * dpad * dpad * tile_frac * split
+        out[f"{prec}_call_ms"] = round(t * 1e3, 4)
+        out[f"{prec}_kernels_ms"] = round(t_all * 1e3, 4)
+        out[f"{prec}_tensor_tflops"] = round(performed / t_all / 1e12, 1)
+        out[f"{prec}_frac_of_tf32_peak"] = round(performed / t_all / 1e12 / peak, 3)
+    acc = torch.zeros((d, d), device=device)
+    torch.backends.cuda.matmul.allow_tf32 = False
     t = _time(lambda: acc.addmm_(x.T, x * w.unsqueeze(1)), args.steps, args.warmup)
-    out["torch_fp32_addmm_ms"] = t * 1e3
+    out["torch_fp32_addmm_ms"] = round(t * 1e3, 4)
     print(json.dumps(out))
 
 
@@ -374,6 +399,8 @@ def main():
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
+    ap.add_argument("--tokens", type=int, default=TOKENS, help="hessian case: samples per call")
+    ap.add_argument("--dim", type=int, default=HIDDEN, help="hessian case: sample width")
     args = ap.parse_args()
     world, rank, local = _dist()
     if args.case == "viterbi":

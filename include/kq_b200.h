@@ -146,13 +146,30 @@ int kq_trace_abt(const float* A, const float* B, const float* D, int64_t M, int6
 /*
  * C = alpha * A B^T + beta * C on the tensor cores (tcgen05 kind::tf32, TMA
  * fed, TMEM accumulator).  Same shape rules as kq_trace_abt; C [M x N] with
- * row stride ldc.  Used for the Hessian accumulation sum_t w_t x_t x_t^T that
- * kquant/capture.py:713-730 (_accumulate_hessian) performs with FP32 addmm;
- * callers wanting FP32-grade accuracy issue three calls on TF32 hi/lo
- * splits (hi*hi + hi*lo + lo*hi).
+ * row stride ldc.  The accumulator is drained into fp32 registers every
+ * 128 K values, so with TF32-exact operands the result has fp32-GEMM
+ * accuracy.  *err is set to 1 if an internal wait timed out.
  */
 int kq_gemm_abt_tf32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t Kd, int64_t ldc,
                      float alpha, float beta, int* err, void* stream);
+
+/*
+ * Hessian accumulation, replacing the chunk body of
+ * kquant/capture.py:713-730 (_accumulate_hessian, accumulator.addmm_(x.T,
+ * x * w[:, None]) in FP32):
+ *     H[d x d] (row stride ldh) += x^T diag(w) x
+ * for samples x [tokens x d] (row stride ldx) and weights w [tokens] (NULL:
+ * all ones).  One operand kernel (transpose, weighting, TF32 hi/lo split)
+ * and one tcgen05 launch over the upper-triangle tiles, mirrored, so H
+ * stays exactly symmetric.  split = 3: hi*hi + hi*lo + lo*hi (fp32-grade
+ * accuracy, what the FP32 addmm of the reference gives); split = 1: TF32
+ * operands.  Any tokens >= 0 and dim >= 1; the workspace holds the padded
+ * operands, kq_hessian_workspace_bytes(tokens, dim, split) bytes, 16-byte
+ * aligned (0 = invalid arguments).
+ */
+size_t kq_hessian_workspace_bytes(int64_t tokens, int64_t dim, int split);
+int kq_accumulate_hessian(const float* x, const float* w, int64_t tokens, int64_t dim, int64_t ldx, float* H,
+                          int64_t ldh, int split, void* workspace, size_t workspace_bytes, int* err, void* stream);
 
 /*
  * Weight load: bf16 [rows x cols] (row stride ld_src elements; HF [out, in])

@@ -36,6 +36,8 @@ EXPORTED = (
     "kq_trace_abt",
     "kq_bf16_to_f32_transposed",
     "kq_gemm_abt_tf32",
+    "kq_hessian_workspace_bytes",
+    "kq_accumulate_hessian",
 )
 
 _lib = None
@@ -74,9 +76,12 @@ def load() -> ctypes.CDLL:
         L.kq_trace_abt.argtypes = [P, P, P, I64, I64, I64, I64, P, P, P]
         L.kq_bf16_to_f32_transposed.argtypes = [P, I64, I64, I64, P, P, P]
         L.kq_gemm_abt_tf32.argtypes = [P, P, P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_float, P, P]
+        L.kq_hessian_workspace_bytes.argtypes = [I64, I64, I]
+        L.kq_hessian_workspace_bytes.restype = SZ
+        L.kq_accumulate_hessian.argtypes = [P, P, I64, I64, I64, P, I64, I, P, SZ, P, P]
         for name in EXPORTED:
             f = getattr(L, name)
-            if name not in ("kq_last_error", "kq_viterbi_workspace_bytes") and f.restype is ctypes.c_int:
+            if name not in ("kq_last_error", "kq_viterbi_workspace_bytes", "kq_hessian_workspace_bytes") and f.restype is ctypes.c_int:
                 f.restype = I
         _lib = L
         return L
@@ -312,3 +317,35 @@ def gemm_abt_tf32(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, alpha: floa
                                        float(beta), err.data_ptr(), _stream(A.device)), "kq_gemm_abt_tf32")
     stats.launches += 1
     _trace_errors.append(err)
+
+
+def hessian_workspace_bytes(tokens: int, dim: int, split: int) -> int:
+    return int(load().kq_hessian_workspace_bytes(int(tokens), int(dim), int(split)))
+
+
+def accumulate_hessian(x: torch.Tensor, w: torch.Tensor | None, H: torch.Tensor, split: int = 3,
+                       workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """H += x^T diag(w) x in place (x [T, d] fp32, w [T] fp32 or None, H [d, d] fp32), symmetric result.
+
+    split=3: 3xTF32 (fp32-grade accuracy); split=1: TF32 operands.  Returns the workspace for reuse.
+    """
+    _cuda(x, "x", torch.float32)
+    _cuda(H, "H", torch.float32)
+    T, d = x.shape
+    if H.shape != (d, d):
+        raise ValueError("accumulate_hessian: H must be [d, d]")
+    if w is not None:
+        _cuda(w, "w", torch.float32)
+        if w.shape != (T,):
+            raise ValueError("accumulate_hessian: w must be [T]")
+    need = hessian_workspace_bytes(T, d, split)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
+    err = torch.zeros((), dtype=torch.int32, device=x.device)
+    with torch.cuda.device(x.device):
+        _check(load().kq_accumulate_hessian(x.data_ptr(), 0 if w is None else w.data_ptr(), T, d, d, H.data_ptr(),
+                                            d, int(split), workspace.data_ptr(), workspace.numel(), err.data_ptr(),
+                                            _stream(x.device)), "kq_accumulate_hessian")
+    stats.launches += 2
+    _trace_errors.append(err)
+    return workspace
