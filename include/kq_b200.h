@@ -94,6 +94,26 @@ int kq_quantize_tiles_procedural(const float* tiles, float* out_vals, uint16_t* 
                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * One 16-row step of the block-LDLQ traversal, fused around the Viterbi:
+ * for a batch of row-major [size_k x size_n] fp32 matrices,
+ *     tiles   = tensor-core-ordered 16x16 tiles of W[:, r0:r0+16] + comp
+ *     What[:, r0:r0+16], enc[:, r0/16] = Viterbi(tiles)   (rows in W's layout)
+ *     err[:, r0:r0+16] = W[:, r0:r0+16] - What[:, r0:r0+16]
+ * comp [batch][16][size_n] is the LDLQ feedback of the step, enc
+ * [batch][size_k/16][size_n/16][256] the 16-bit states.  Replaces the
+ * tile gather / quantize_tiles / scatter sequence of one step of
+ * kquant/exl3_encoder_backend.py:389-505 (ldlq); the arithmetic (one fp32
+ * add, the Viterbi, one fp32 subtract) is the reference's.  Same labels,
+ * K, context and workspace rules as kq_viterbi_encode with
+ * n_tiles = batch * size_n / 16.  max_ctas > 0 caps the grid (each CTA
+ * then loops over tile pairs), leaving the other SMs to concurrent work on
+ * other streams; 0 uses every SM.
+ */
+int kq_ldlq_step_encode(const float* W, const float* comp, int64_t batch, int64_t size_k, int64_t size_n,
+                        int64_t r0, int K, const uint16_t* labels, int tailbite_ctx, float* wq, float* err,
+                        uint16_t* enc, int max_ctas, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Pack the low K bits of every state into 16*K uint16 words per tile in the
  * native EXL word order: MSB-first 16-symbol groups, then adjacent words
  * swapped (SWAP16).  Replaces ext.pack_trellis

@@ -38,6 +38,7 @@ EXPORTED = (
     "kq_gemm_abt_tf32",
     "kq_hessian_workspace_bytes",
     "kq_accumulate_hessian",
+    "kq_ldlq_step_encode",
 )
 
 _lib = None
@@ -76,6 +77,7 @@ def load() -> ctypes.CDLL:
         L.kq_trace_abt.argtypes = [P, P, P, I64, I64, I64, I64, P, P, P]
         L.kq_bf16_to_f32_transposed.argtypes = [P, I64, I64, I64, P, P, P]
         L.kq_gemm_abt_tf32.argtypes = [P, P, P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_float, P, P]
+        L.kq_ldlq_step_encode.argtypes = [P, P, I64, I64, I64, I64, I, P, I, P, P, P, I, P, SZ, P]
         L.kq_hessian_workspace_bytes.argtypes = [I64, I64, I]
         L.kq_hessian_workspace_bytes.restype = SZ
         L.kq_accumulate_hessian.argtypes = [P, P, I64, I64, I64, P, I64, I, P, SZ, P, P]
@@ -119,32 +121,57 @@ class _Stats:
         self.launches = 0
         self.timing = timing
         self.events = []
+        self.base = None
+        if timing and torch.cuda.is_available():
+            self.base = torch.cuda.Event(enable_timing=True)
+            self.base.record()
 
     def viterbi_summary(self):
-        """(launches, total seconds, total tiles, total relaxations) of timed Viterbi launches."""
+        """(launches, busy seconds, total tiles, total relaxations, summed launch seconds) of timed Viterbi launches.
+
+        Launches on concurrent streams overlap, so the busy time is the length of
+        the union of their [start, end] intervals (the summed durations count the
+        overlap twice).
+        """
         total_s, tiles, relax = 0.0, 0, 0
+        spans = []
         for a, b, n, c in self.events:
             b.synchronize()
             total_s += a.elapsed_time(b) / 1e3
+            if self.base is not None:
+                spans.append((self.base.elapsed_time(a), self.base.elapsed_time(b)))
             tiles += n
             relax += n * (2 * c + 256) * 65536
-        return len(self.events), total_s, tiles, relax
+        busy = total_s
+        if spans:
+            busy, cur_a, cur_b = 0.0, None, None
+            for a, b in sorted(spans):
+                if cur_b is None or a > cur_b:
+                    if cur_b is not None:
+                        busy += cur_b - cur_a
+                    cur_a, cur_b = a, b
+                else:
+                    cur_b = max(cur_b, b)
+            busy = (busy + cur_b - cur_a) / 1e3
+        return len(self.events), busy, tiles, relax, total_s
 
 
 stats = _Stats()
 
 
-# Workspace: one growing uint8 buffer per device, reused across calls on the
-# current stream (calls on one stream are ordered, so reuse is safe).
-_workspaces: dict[int, torch.Tensor] = {}
+# Workspace: one growing uint8 buffer per (device, stream), reused across
+# calls on that stream (calls on one stream are ordered, so reuse is safe;
+# concurrent streams get their own buffers).
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _workspaces.get(idx)
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _workspaces[idx] = ws
+        _workspaces[key] = ws
     return ws
 
 
@@ -349,3 +376,36 @@ def accumulate_hessian(x: torch.Tensor, w: torch.Tensor | None, H: torch.Tensor,
     stats.launches += 2
     _trace_errors.append(err)
     return workspace
+
+
+def ldlq_step_encode(W: torch.Tensor, comp: torch.Tensor, r0: int, K: int, labels: torch.Tensor,
+                     tailbite_context: int, wq: torch.Tensor, err: torch.Tensor, enc: torch.Tensor,
+                     max_ctas: int = 0) -> None:
+    """One fused LDLQ step: Viterbi of the tiles of W[:, r0:r0+16] + comp; writes wq, err and enc rows in place.
+
+    W, wq, err [B, k, n] fp32; comp [B, 16, n] fp32; enc [B, k/16, n/16, 256] int16 (all contiguous, CUDA).
+    max_ctas > 0 caps the grid (the rest of the SMs stay free for other streams).
+    """
+    for name, t in (("W", W), ("comp", comp), ("wq", wq), ("err", err)):
+        _cuda(t, name, torch.float32)
+    _cuda(enc, "enc", torch.int16)
+    _cuda(labels, "labels", torch.int16)
+    B, k, n = W.shape
+    if comp.shape != (B, 16, n) or wq.shape != W.shape or err.shape != W.shape or enc.shape != (B, k // 16, n // 16, 256):
+        raise ValueError("ldlq_step_encode: inconsistent shapes")
+    dev = W.device
+    with torch.cuda.device(dev):
+        need = viterbi_workspace_bytes(K, B * (n // 16))
+        ws = workspace(dev, need)
+        if stats.timing:
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+        _check(load().kq_ldlq_step_encode(W.data_ptr(), comp.data_ptr(), B, k, n, int(r0), int(K), labels.data_ptr(),
+                                          int(tailbite_context), wq.data_ptr(), err.data_ptr(), enc.data_ptr(),
+                                          int(max_ctas), ws.data_ptr(), ws.numel(), _stream(dev)),
+               "kq_ldlq_step_encode")
+        if stats.timing:
+            b.record()
+            stats.events.append((a, b, B * (n // 16), int(tailbite_context)))
+    stats.launches += 1

@@ -211,11 +211,64 @@ __device__ __forceinline__ void run_steps(
     }
 }
 
-template <int K>
+// Tile I/O policies.  load(tile, j) returns element j (trellis order) of a
+// tile; store(tile, j, state, value) receives its encoded state and value.
+//
+// FlatIO: tiles [n][256] already in trellis order, outputs alike.
+struct FlatIO {
+    const float* __restrict__ tiles;
+    float* __restrict__ vals;
+    uint16_t* __restrict__ states;
+    __device__ __forceinline__ float load(int64_t tile, int j) const { return tiles[tile * 256 + j]; }
+    __device__ __forceinline__ void store(int64_t tile, int j, uint16_t sv, float v) const {
+        states[tile * 256 + j] = sv;
+        vals[tile * 256 + j] = v;
+    }
+};
+
+// StepIO: one 16-row LDLQ step of a batch of [k x n] matrices (row-major,
+// contiguous): tile t is batch b = t / tiles_n, tile column c = t % tiles_n
+// of rows r0..r0+15.  Trellis position j = 8 m + s of a tile holds row
+// 2 (m % 4) + (s & 1) + 8 ((s >> 1) & 1), column m / 4 + 8 (s >> 2) (the
+// tensor-core order of kquant/exl3_encoder_backend.py:27-50).  Loads
+// W + comp, stores What = value, E = W - value and the state into
+// enc [b][r0 / 16][c][j].
+struct StepIO {
+    const float* __restrict__ W;
+    const float* __restrict__ comp;    // [batch][16][n]
+    float* __restrict__ wq;
+    float* __restrict__ err;
+    uint16_t* __restrict__ enc;        // [batch][k / 16][n / 16][256]
+    int64_t size_k, size_n, r0;
+    int tiles_n;
+    __device__ __forceinline__ void locate(int64_t tile, int j, int64_t& wi, int64_t& ci) const {
+        const int m = j >> 3, s = j & 7;
+        const int row = 2 * (m & 3) + (s & 1) + 8 * ((s >> 1) & 1);
+        const int col = (m >> 2) + 8 * (s >> 2);
+        const int64_t b = tile / tiles_n, c = tile - b * tiles_n;
+        const int64_t x = c * 16 + col;
+        wi = (b * size_k + r0 + row) * size_n + x;
+        ci = (b * 16 + row) * size_n + x;
+    }
+    __device__ __forceinline__ float load(int64_t tile, int j) const {
+        int64_t wi, ci;
+        locate(tile, j, wi, ci);
+        return W[wi] + comp[ci];
+    }
+    __device__ __forceinline__ void store(int64_t tile, int j, uint16_t sv, float v) const {
+        int64_t wi, ci;
+        locate(tile, j, wi, ci);
+        wq[wi] = v;
+        err[wi] = W[wi] - v;
+        const int64_t b = tile / tiles_n, c = tile - b * tiles_n;
+        enc[((b * (size_k >> 4) + (r0 >> 4)) * tiles_n + c) * 256 + j] = sv;
+    }
+};
+
+template <int K, class IO>
 __global__ void __launch_bounds__(kThreads, 1)
-pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __restrict__ labels32,
-            const __half* __restrict__ labels16, int C, int njobs,
-            float* __restrict__ out_vals, uint16_t* __restrict__ out_states, uint8_t* __restrict__ decisions)
+pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
+            const __half* __restrict__ labels16, int C, int njobs, uint8_t* __restrict__ decisions)
 {
     using M = PairMap<K>;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -251,7 +304,7 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
         const int t = tid >> 8, r = tid & 255;
         int64_t tile = 2 * q + t;
         if (tile >= n_tiles) tile = 2 * q;
-        reinterpret_cast<__half*>(wsh + j * 256 + r)[t] = __float2half_rn(tiles[tile * 256 + r]);
+        reinterpret_cast<__half*>(wsh + j * 256 + r)[t] = __float2half_rn(io.load(tile, r));
     };
 
     int phase[kJobs], step[kJobs], par[kJobs];
@@ -322,8 +375,7 @@ pair_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
                     const int64_t tile = 2 * pair[j] + t;
                     if (tile < n_tiles) {
                         const uint16_t sv = enc[(j * 2 + t) * 256 + r];
-                        out_states[tile * 256 + r] = sv;
-                        out_vals[tile * 256 + r] = __half2float(labels16[sv]);
+                        io.store(tile, r, sv, __half2float(labels16[sv]));
                     }
                     if (qnext[j] < n_pairs) load_pair(j, qnext[j]);
                 }
@@ -499,6 +551,17 @@ void pair_grid(int64_t n, int sms, int& grid, int& njobs) {
     else { grid = sms; njobs = kJobs; }
 }
 
+template <int K, class IO>
+int pair_run(const IO& io, int64_t n, const uint16_t* labels, int C, int grid, int njobs, uint8_t* dec,
+             cudaStream_t stream) {
+    const size_t sm = pair_smem_bytes<K>();
+    cudaError_t e = cudaFuncSetAttribute(pair_kernel<K, IO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
+    pair_kernel<K, IO><<<grid, kThreads, sm, stream>>>(io, n, reinterpret_cast<const uint32_t*>(labels),
+                                                       reinterpret_cast<const __half*>(labels), C, njobs, dec);
+    return check_launch("pair_kernel");
+}
+
 }  // namespace
 
 size_t pair_decision_bytes(int K, int64_t n, int sms) {
@@ -520,13 +583,7 @@ int pair_launch(const float* tiles, int64_t n, const uint16_t* labels, int C, fl
         set_error("viterbi workspace too small: %zu < %zu", ws_bytes, need);
         return KQ_ERR_WORKSPACE;
     }
-    const size_t sm = pair_smem_bytes<K>();
-    cudaError_t e = cudaFuncSetAttribute(pair_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
-    pair_kernel<K><<<grid, kThreads, sm, stream>>>(tiles, n, reinterpret_cast<const uint32_t*>(labels),
-                                                   reinterpret_cast<const __half*>(labels), C, njobs, vals, states,
-                                                   ws);
-    return check_launch("pair_kernel");
+    return pair_run<K>(FlatIO{tiles, vals, states}, n, labels, C, grid, njobs, ws, stream);
 }
 
 template int pair_launch<2>(const float*, int64_t, const uint16_t*, int, float*, uint16_t*, uint8_t*, size_t,
@@ -554,13 +611,34 @@ static int pair_launch_bounded(const float* tiles, int64_t n, const uint16_t* la
         return KQ_ERR_WORKSPACE;
     }
     const int njobs = pairs > grid ? kJobs : 1;
-    const size_t sm = pair_smem_bytes<K>();
-    cudaError_t e = cudaFuncSetAttribute(pair_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
-    pair_kernel<K><<<(int)grid, kThreads, sm, stream>>>(tiles, n, reinterpret_cast<const uint32_t*>(labels),
-                                                        reinterpret_cast<const __half*>(labels), C, njobs, vals,
-                                                        states, dec);
-    return check_launch("pair_kernel");
+    return pair_run<K>(FlatIO{tiles, vals, states}, n, labels, C, (int)grid, njobs, dec, stream);
+}
+
+// One LDLQ step (StepIO) through the same kernel and grid policy as pair_launch.
+template <int K>
+int step_launch(const StepIO& io, int64_t n, const uint16_t* labels, int C, int max_ctas, uint8_t* ws,
+                size_t ws_bytes, cudaStream_t stream) {
+    int sms = 0;
+    if (int rc = sm_count(&sms)) return rc;
+    if (max_ctas > 0 && max_ctas < sms) sms = max_ctas;
+    int grid, njobs;
+    pair_grid<K>(n, sms, grid, njobs);
+    const size_t need = (size_t)grid * kJobs * 256 * PairMap<K>::ROW_BYTES;
+    if (ws_bytes < need) {
+        set_error("viterbi workspace too small: %zu < %zu", ws_bytes, need);
+        return KQ_ERR_WORKSPACE;
+    }
+    return pair_run<K>(io, n, labels, C, grid, njobs, ws, stream);
+}
+
+int ldlq_step_encode(const StepIO& io, int64_t n, int K, const uint16_t* labels, int C, int max_ctas, uint8_t* ws,
+                     size_t ws_bytes, cudaStream_t stream) {
+    switch (K) {
+    case 2: return step_launch<2>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
+    case 3: return step_launch<3>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
+    case 4: return step_launch<4>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
+    default: set_error("viterbi: K must be 2, 3 or 4 (got %d)", K); return KQ_ERR_ARG;
+    }
 }
 
 int viterbi_encode_bounded(const float* tiles, int64_t n, int K, const uint16_t* labels, int C, float* vals,
@@ -574,3 +652,29 @@ int viterbi_encode_bounded(const float* tiles, int64_t n, int K, const uint16_t*
 }
 
 }  // namespace kq
+
+extern "C" int kq_ldlq_step_encode(const float* W, const float* comp, int64_t batch, int64_t size_k, int64_t size_n,
+                                   int64_t r0, int K, const uint16_t* labels, int tailbite_ctx, float* wq,
+                                   float* err, uint16_t* enc, int max_ctas, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    using namespace kq;
+    if (!W || !comp || !labels || !wq || !err || !enc) { set_error("kq_ldlq_step_encode: null pointer"); return KQ_ERR_ARG; }
+    if (batch <= 0 || size_k <= 0 || size_n <= 0 || size_k % 16 || size_n % 16 || r0 < 0 || r0 % 16 ||
+        r0 + 16 > size_k) {
+        set_error("kq_ldlq_step_encode: bad shape (batch=%lld k=%lld n=%lld r0=%lld)", (long long)batch,
+                  (long long)size_k, (long long)size_n, (long long)r0);
+        return KQ_ERR_ARG;
+    }
+    if (tailbite_ctx < 1 || tailbite_ctx > 128) {
+        set_error("tailbite_context must be in 1..128 (got %d)", tailbite_ctx);
+        return KQ_ERR_ARG;
+    }
+    if (((uintptr_t)labels & 3) || ((uintptr_t)workspace & 15)) {
+        set_error("kq_ldlq_step_encode: labels must be 4-byte and workspace 16-byte aligned");
+        return KQ_ERR_ALIGN;
+    }
+    if (size_n / 16 > 0x7FFFFFFF) { set_error("kq_ldlq_step_encode: n too large"); return KQ_ERR_ARG; }
+    StepIO io{W, comp, wq, err, enc, size_k, size_n, r0, (int)(size_n / 16)};
+    return ldlq_step_encode(io, batch * (size_n / 16), K, labels, tailbite_ctx, max_ctas, static_cast<uint8_t*>(workspace),
+                            workspace_bytes, static_cast<cudaStream_t>(stream));
+}

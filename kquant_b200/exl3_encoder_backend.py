@@ -504,10 +504,28 @@ def _quantize_step_tiles(tiles: torch.Tensor, plan: _RatePlan, step_tile: int, q
     return q, idx
 
 
-def _ldlq_traverse(weights, Ls, quant_args, plan: _RatePlan, *, buffer_rows: int, tf32: bool,
-                   process_begin: int = 0, process_end: int | None = None, state=None,
-                   source_indices: torch.Tensor | None = None, pb=None):
+def _drive(gen):
+    while True:
+        try:
+            next(gen)
+        except StopIteration as done:
+            return done.value
+
+
+def _ldlq_traverse(weights, Ls, quant_args, plan: _RatePlan, **kw):
+    """Run :func:`_ldlq_traverse_steps` to completion; returns (What, enc, P)."""
+    return _drive(_ldlq_traverse_steps(weights, Ls, quant_args, plan, **kw))
+
+
+def _ldlq_traverse_steps(weights, Ls, quant_args, plan: _RatePlan, *, buffer_rows: int, tf32: bool,
+                         process_begin: int = 0, process_end: int | None = None, state=None,
+                         source_indices: torch.Tensor | None = None, pb=None, launch_ctl: dict | None = None):
     """Backward block-LDLQ over rows [process_begin, process_end) of a batch.
+
+    A generator: it yields after enqueueing each 16-row step (so several
+    independent traversals can be interleaved on their own streams) and
+    returns (What, enc, P).  ``launch_ctl["max_ctas"]``, read at every step,
+    caps the grid of the fused step's Viterbi launch.
 
     weights [S, k, n] and Ls [S, k, k] are sources; members read source
     ``source_indices[b]`` (identity when None).  For every 16-row step
@@ -541,6 +559,37 @@ def _ldlq_traverse(weights, Ls, quant_args, plan: _RatePlan, *, buffer_rows: int
         return v if source_indices is None else v.index_select(0, source_indices)
 
     progress = 0
+    fused = (state is None and source_indices is None and process_begin == 0 and process_end == size_k
+             and plan.uniform is not None and len(quant_args.get("devices", [dev])) == 1
+             and weights.is_contiguous() and weights.dtype == torch.float32)
+    if fused:
+        # Fused steps: the Viterbi launch gathers W + comp into tiles and
+        # scatters What, E = W - What and the states itself.
+        bits = plan.uniform
+        if bits not in (2, 3, 4):
+            raise ValueError("the trellis kernel supports K2--K4")
+        ctx = int(quant_args.get("tailbite_context", 128))
+        if not 1 <= ctx <= 128:
+            raise ValueError("tailbite_context must be in 1..128")
+        kind, lut = _tile_codebook(quant_args, bits)
+        labels = _labels_for(dev, bits, kind, lut)
+        E = torch.empty_like(weights)
+        for end in range(process_end, process_begin, -buffer_rows):
+            begin = end - buffer_rows
+            for local_end in range(buffer_rows, 0, -16):
+                r0 = begin + local_end - 16
+                r1 = r0 + 16
+                comp = _baddbmm_ldlq(P[:, r0:r1], Ls[:, r1:end, r0:r1].transpose(1, 2), E[:, r1:end], tf32=tf32)
+                _native.ldlq_step_encode(weights, comp.contiguous(), r0, bits, labels, ctx, wq, E, enc,
+                                         max_ctas=launch_ctl.get("max_ctas", 0) if launch_ctl else 0)
+                if pb:
+                    progress += 1
+                    pb.update(progress)
+                yield
+            if begin:
+                _baddbmm_ldlq(P[:, :begin], Ls[:, begin:end, :begin].transpose(1, 2), E[:, begin:end], tf32=tf32,
+                              inplace=True)
+        return wq, enc, P
     for end in range(process_end, process_begin, -buffer_rows):
         begin = end - buffer_rows
         for local_end in range(buffer_rows, 0, -16):
@@ -559,6 +608,7 @@ def _ldlq_traverse(weights, Ls, quant_args, plan: _RatePlan, *, buffer_rows: int
             if pb:
                 progress += 1
                 pb.update(progress)
+            yield
         if begin:
             err = src(weights, slice(begin, end)) - wq[:, begin:end]
             ldl = src(Ls, slice(begin, end), slice(0, begin))
@@ -1435,13 +1485,13 @@ def quantize_qsrt_batch(weights: list[torch.Tensor], H_datas: list[dict], quant_
     return results
 
 
-def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], quant_args_list: list[dict],
-                           progress_str: str | None = None, verbose: bool = False):
-    """Encode same-K linears together (kquant/exl3_encoder_backend.py:2538-2765).
+def _uniform_prepare(weights: list[torch.Tensor], H_datas: list[dict], quant_args_list: list[dict],
+                     verbose: bool):
+    """Phase 1 of quantize_uniform_batch: H finalisation, regularisation, global scale.
 
-    A shared H object concatenates the regularised weights along N into one
-    LDLQ traversal; distinct Hessians of one shape go through ldlq_batched.
-    Returns [(proxy, out_tensors)] per input and updates each quant_args.
+    Consumes the RNG exactly as the reference does (reseeded per matrix).
+    Returns the batch state; ``state["ldlq"]`` is None when every member fell
+    back (``state["results"]`` is then complete).
     """
     if any("mixed_rate_axis" in a or "mixed_tile_bits" in a for a in quant_args_list):
         raise ValueError("mixed-rate LDLQ is currently supported by quantize_qsrt, not the same-K batch API")
@@ -1467,8 +1517,10 @@ def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], qua
     for t in range(n_t):
         if finalized[t] is None:
             results[t] = quantize_qsrt(weights[t], H_datas[t], quant_args_list[t], False, None, verbose)[1:]
+    state = {"results": results, "H_datas": H_datas, "quant_args_list": quant_args_list, "device": device,
+             "shared_H": shared_H, "finalized": finalized, "batch": batch, "ldlq": None}
     if not batch:
-        return results
+        return state
     regs = {}
     for t in batch:
         qa = quant_args_list[t]
@@ -1492,25 +1544,52 @@ def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], qua
         else:
             regs[t][1] /= g
         g_scales[t] = g
+    # LDLQ operands: a shared H concatenates the members along N into one
+    # traversal; distinct Hessians of one shape are stacked.
     if shared_H:
         L = finalized[batch[0]][1].to(device)
         widths = [regs[t][0].shape[1] for t in batch]
-        cat = torch.cat([regs[t][0] for t in batch], dim=1)
-        for t in batch:
-            regs[t][0] = None
-        wq_cat, enc_cat = ldlq(cat, L, qa0)
-        del L
-        wrs = list(torch.split(cat, widths, dim=1))
-        wqs = list(torch.split(wq_cat, widths, dim=1))
-        encs = list(torch.split(enc_cat, [w // 16 for w in widths], dim=1))
+        W = torch.cat([regs[t][0] for t in batch], dim=1).unsqueeze(0)
+        Ls = L.unsqueeze(0)
     else:
+        widths = None
         Ls = torch.stack([finalized[t][1].to(device) for t in batch])
-        stack = torch.stack([regs[t][0] for t in batch])
-        for t in batch:
-            regs[t][0] = None
-        wq_stack, enc_stack = ldlq_batched(stack, Ls, qa0)
-        del Ls
-        wrs, wqs, encs = list(stack.unbind(0)), list(wq_stack.unbind(0)), list(enc_stack.unbind(0))
+        W = torch.stack([regs[t][0] for t in batch])
+    for t in batch:
+        regs[t][0] = None
+    _, size_k, size_n = W.shape
+    assert size_k % 16 == 0 and size_n % 128 == 0
+    kind, lut = _tile_codebook(qa0, int(qa0["K"]))
+    _labels_for(device, int(qa0["K"]), kind, lut)    # built before any traversal stream uses it
+    state.update(regs=regs, g_scales=g_scales, widths=widths, ldlq=(W, Ls))
+    return state
+
+
+def _uniform_traversal(state: dict, launch_ctl: dict | None = None):
+    """Phase 2: the LDLQ traversal of a prepared batch, as a step generator returning (What, enc)."""
+    W, Ls = state["ldlq"]
+    qa0 = state["quant_args_list"][0]
+    plan = _RatePlan(int(qa0["K"]), None, W.shape[0], W.shape[2] // 16, W.device)
+    wq, enc, _ = yield from _ldlq_traverse_steps(W, Ls, qa0, plan, buffer_rows=_buffer_rows(qa0, W.shape[1]),
+                                                 tf32=bool(qa0.get("ldlq_tf32", False)), launch_ctl=launch_ctl)
+    return wq, enc
+
+
+def _uniform_finish(state: dict, wq: torch.Tensor, enc: torch.Tensor):
+    """Phase 3: proxy, optional error metrics, packing and outputs of a traversed batch."""
+    results, batch, regs = state["results"], state["batch"], state["regs"]
+    quant_args_list, H_datas, finalized = state["quant_args_list"], state["H_datas"], state["finalized"]
+    device, shared_H, g_scales = state["device"], state["shared_H"], state["g_scales"]
+    W, _ = state["ldlq"]
+    state["ldlq"] = None
+    if shared_H:
+        widths = state["widths"]
+        wrs = list(torch.split(W[0], widths, dim=1))
+        wqs = list(torch.split(wq[0], widths, dim=1))
+        encs = list(torch.split(enc[0], [w // 16 for w in widths], dim=1))
+    else:
+        wrs, wqs, encs = list(W.unbind(0)), list(wq.unbind(0)), list(enc.unbind(0))
+    del W, wq, enc
     Hd = None
     for bi, t in enumerate(batch):
         qa = quant_args_list[t]
@@ -1547,6 +1626,147 @@ def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], qua
         qa.update({"apply_out_scales": apply_out, "g_scale": g_scales[t], "q_fallback": False})
         results[t] = (proxy, out)
     return results
+
+
+def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], quant_args_list: list[dict],
+                           progress_str: str | None = None, verbose: bool = False):
+    """Encode same-K linears together (kquant/exl3_encoder_backend.py:2538-2765).
+
+    A shared H object concatenates the regularised weights along N into one
+    LDLQ traversal; distinct Hessians of one shape go through one batched
+    traversal.  Returns [(proxy, out_tensors)] per input and updates each
+    quant_args.
+    """
+    state = _uniform_prepare(weights, H_datas, quant_args_list, verbose)
+    if state["ldlq"] is None:
+        return state["results"]
+    devices = quant_args_list[0]["devices"]
+    _sync(devices)
+    with torch.cuda.stream(get_quant_stream(state["device"])):
+        wq, enc = _drive(_uniform_traversal(state))
+    _sync(devices)
+    return _uniform_finish(state, wq, enc)
+
+
+def quantize_uniform_batches(groups, verbose: bool = False):
+    """Several independent ``quantize_uniform_batch`` calls with overlapped LDLQ traversals.
+
+    ``groups`` is a list of (weights, H_datas, quant_args_list).  Results
+    equal the sequential calls bit for bit (same RNG seeding, same
+    arithmetic, same launches): the preparation phases run in order, then
+    the traversals advance step by step on their own CUDA streams, then the
+    outputs are built in order.  Returns one result list per group.
+
+    Schedule.  A Viterbi launch of n tiles runs in ceil(n / (2 SMs)) waves of
+    one tile pair per SM, so a step of n <= 2 SMs tiles leaves
+    SMs - ceil(n / 2) SMs idle for its whole duration.  The primary
+    traversal (longest critical path among those that fit one wave) runs on
+    a high-priority stream with full grids; the others run one after another
+    on a low-priority stream with their grid capped at the primary's idle
+    SMs for the steps predicted to overlap it, and with full grids after
+    that.  Groups spanning several devices, or with no idle SMs to fill, run
+    sequentially.
+    """
+    groups = [(list(w), list(h), list(q)) for w, h, q in groups]
+    if any(len(q[0]["devices"]) > 1 for _, _, q in groups) or len(groups) < 2:
+        return [quantize_uniform_batch(w, h, q, None, verbose) for w, h, q in groups]
+    states = [_uniform_prepare(w, h, q, verbose) for w, h, q in groups]
+    live = [i for i, st in enumerate(states) if st["ldlq"] is not None]
+    out = {}
+    if live:
+        dev = states[live[0]]["device"]
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        shape = {i: states[i]["ldlq"][0].shape for i in live}
+        tiles = {i: shape[i][0] * shape[i][2] // 16 for i in live}
+        steps = {i: shape[i][1] // 16 for i in live}
+        one_wave = [i for i in live if tiles[i] <= 2 * sms]
+        primary = max(one_wave, key=lambda i: steps[i]) if one_wave else None
+        spare = sms - (tiles[primary] + 1) // 2 if primary is not None else 0
+        if (primary is None or spare < 4 or len(live) < 2
+                or any(str(states[i]["device"]) != str(dev) for i in live)):
+            for i in live:
+                _sync(states[i]["quant_args_list"][0]["devices"])
+                with torch.cuda.stream(get_quant_stream(states[i]["device"])):
+                    out[i] = _drive(_uniform_traversal(states[i]))
+        else:
+            out = _overlap_traversals(states, live, primary, steps, tiles, sms, spare, dev)
+    results = []
+    for i, st in enumerate(states):
+        results.append(st["results"] if st["ldlq"] is None else _uniform_finish(st, *out[i]))
+    return results
+
+
+@lru_cache
+def _overlap_streams(device):
+    """(high, low) priority streams of a device, created once so the caching
+    allocator's per-stream pools are reused from call to call."""
+    return torch.cuda.Stream(device=device, priority=-1), torch.cuda.Stream(device=device, priority=0)
+
+
+# Fraction of the primary's predicted duration that capped secondary steps
+# may fill; the margin absorbs prediction error (a capped step left over
+# after the primary ends would run alone on a few SMs).
+OVERLAP_BUDGET = 1.0
+
+
+def _overlap_traversals(states, live, primary, steps, tiles, sms, spare, dev):
+    """Drive the traversals of quantize_uniform_batches; returns {group: (What, enc)}.
+
+    1. Primary steps (high priority, full grid) and capped secondary steps (low
+       priority, grid = the primary's idle SMs) are enqueued in order of their
+       predicted finish, until the capped budget is used.
+    2. The remaining primary steps are enqueued and their end is recorded.
+    3. The low stream waits for that event, then runs the remaining
+       secondary steps with full grids, so they never compete with the primary.
+    """
+    _sync([str(dev)])
+    hi, lo = _overlap_streams(dev)
+    start = torch.cuda.current_stream(dev).record_event()
+    hi.wait_event(start)
+    lo.wait_event(start)
+    out = {}
+
+    def advance(i, gen, stream):
+        with torch.cuda.device(dev), torch.cuda.stream(stream):
+            try:
+                next(gen)
+                return True
+            except StopIteration as fin:
+                out[i] = fin.value
+                return False
+
+    ctl = {"max_ctas": spare}
+    queue = [i for i in live if i != primary]
+    gens = {i: _uniform_traversal(states[i], ctl) for i in queue}
+    prim = _uniform_traversal(states[primary])
+    budget = OVERLAP_BUDGET * steps[primary]
+    t_hi = t_lo = 0.0
+    prim_live = True
+    while queue and prim_live:
+        cur = queue[0]
+        cost = -(-((tiles[cur] + 1) // 2) // spare)         # pair-rounds of one capped step
+        if t_lo + cost > budget:
+            break
+        if t_hi <= t_lo:
+            prim_live = advance(primary, prim, hi)
+            t_hi += 1
+        else:
+            if advance(cur, gens[cur], lo):
+                t_lo += cost
+            else:
+                queue.pop(0)
+    while prim_live:
+        prim_live = advance(primary, prim, hi)
+    lo.wait_event(hi.record_event())
+    ctl["max_ctas"] = 0
+    for i in queue:
+        while advance(i, gens[i], lo):
+            pass
+    cur_stream = torch.cuda.current_stream(dev)
+    cur_stream.wait_stream(hi)
+    cur_stream.wait_stream(lo)
+    _sync([str(dev)])
+    return out
 
 
 def pack_signs(signs: torch.Tensor, quant_args: dict) -> torch.Tensor:

@@ -118,3 +118,46 @@ def test_quantize_tiles_dispatch_and_errors(cuda_device):
         be.quantize_tiles(tiles, {"K": 3, "devices": [str(dev)], "sqg_e4m3_mode": "other"})
     with pytest.raises(ValueError):
         be.quantize_tiles(tiles[:, :255].contiguous(), {"K": 3, "devices": [str(dev)], "mcg": True})
+
+
+def test_uniform_batches_overlap_equals_sequential(cuda_device):
+    """quantize_uniform_batches (overlapped traversals on prioritised streams) == sequential calls."""
+    dev = cuda_device
+    w1, h13 = _problem(dev, k=512, n=256, seed=21)
+    w3, _ = _problem(dev, k=512, n=256, seed=22)
+    w2, h2 = _problem(dev, k=256, n=512, seed=23)
+
+    def groups():
+        s13 = make_shared_h(512, dev, h13)
+        return [([w1.clone(), w3.clone()], [s13, s13], [_args(dev, seed=1, sv_seed=2), _args(dev, seed=1, sv_seed=3)]),
+                ([w2.clone()], [make_shared_h(256, dev, h2)], [_args(dev, seed=4, sv_seed=5)])]
+
+    seq = [be.quantize_uniform_batch(w, h, q) for w, h, q in groups()]
+    conc = be.quantize_uniform_batches(groups())
+    assert len(conc) == 2
+    for rs, rc in zip(seq, conc):
+        for (ps, os_), (pc, oc) in zip(rs, rc):
+            assert ps == pc
+            for key in ("trellis", "suh", "svh"):
+                assert torch.equal(os_[key], oc[key]), key
+
+
+@pytest.mark.parametrize("B,k,n", [(1, 256, 512), (2, 128, 256)])
+def test_fused_ldlq_step_equals_unfused(cuda_device, B, k, n):
+    """The fused step kernel (kq_ldlq_step_encode) gives the same What/codes as gather + quantize_tiles + scatter."""
+    dev = cuda_device
+    g = torch.Generator(device=dev).manual_seed(B * 1000 + k)
+    W = torch.randn((B, k, n), generator=g, device=dev) * 0.02
+    x = torch.randn((B, 4 * k, k), generator=g, device=dev)
+    H = x.transpose(1, 2) @ x / x.shape[1] + 0.01 * torch.eye(k, device=dev)
+    Ls = torch.stack([torch.linalg.cholesky(h).T.contiguous() for h in H])
+    Ls = Ls / torch.diagonal(Ls, dim1=1, dim2=2).unsqueeze(2)      # unit upper-triangular factor, L^T layout
+    Ls = Ls.transpose(1, 2).contiguous()
+    qa = _args(dev)
+    plan = be._RatePlan(3, None, B, n // 16, dev)
+    fused = be._ldlq_traverse(W, Ls, qa, plan, buffer_rows=128, tf32=False)
+    plain = be._ldlq_traverse(W, Ls, qa, plan, buffer_rows=128, tf32=False,
+                              source_indices=torch.arange(B, device=dev))
+    assert torch.equal(fused[0], plain[0])
+    assert torch.equal(fused[1], plain[1])
+    assert torch.equal(fused[2], plain[2])
