@@ -114,6 +114,45 @@ int kq_ldlq_step_encode(const float* W, const float* comp, int64_t batch, int64_
                         uint16_t* enc, int max_ctas, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * One LDLQ chain item: tiles [tile_col0, tile_col0 + n_tiles) of the 16-row
+ * step r0 of one row-major [size_k x size_n] fp32 matrix W with its LDLQ
+ * state (feedback P, error rows err, What, states enc [size_k/16][size_n/16]
+ * [256]) and block-LDL factor L [size_k x size_k].  The step's feedback rows
+ * are r0+16 .. end-1 (end = the end of the step's 128-row buffer).
+ */
+typedef struct {
+    const float* W;
+    const float* P;
+    const float* L;
+    float* err;
+    float* wq;
+    uint16_t* enc;
+    int64_t size_k, size_n;
+    int64_t r0, end;
+    int64_t tile_col0, n_tiles;
+} kq_chain_item;
+
+#define KQ_CHAIN_MAX_ITEMS 32
+
+/*
+ * One launch of LDLQ steps from up to KQ_CHAIN_MAX_ITEMS independent column
+ * chains, each at its own row position:
+ *     comp = P[r0:r0+16] + L[r0+16:end, r0:r0+16]^T err[r0+16:end]   (fp32)
+ *     tiles = tensor-core-ordered 16x16 tiles of W[r0:r0+16] + comp
+ *     What, enc = Viterbi(tiles);  err[r0:r0+16] = W - What
+ * for the item's tile columns.  The feedback product is computed in the
+ * kernel's tile load (one fp32 fma chain per element, in row order), so a
+ * step is one launch and its result does not depend on which other items
+ * share the launch.  Replaces the per-step feedback + quantize of
+ * kquant/exl3_encoder_backend.py:389-505 (ldlq) / :1495-1583 (ldlq_batched);
+ * the buffer-end update P[:begin] += L^T err stays with the caller.
+ * All items use the same K, labels and context; workspace as
+ * kq_viterbi_encode for the total tile count; max_ctas as kq_ldlq_step_encode.
+ */
+int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int K, const uint16_t* labels, int tailbite_ctx,
+                       int max_ctas, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Pack the low K bits of every state into 16*K uint16 words per tile in the
  * native EXL word order: MSB-first 16-symbol groups, then adjacent words
  * swapped (SWAP16).  Replaces ext.pack_trellis

@@ -39,7 +39,18 @@ EXPORTED = (
     "kq_hessian_workspace_bytes",
     "kq_accumulate_hessian",
     "kq_ldlq_step_encode",
+    "kq_ldlq_chain_step",
 )
+
+KQ_CHAIN_MAX_ITEMS = 32
+
+
+class ChainItem(ctypes.Structure):
+    """kq_chain_item of include/kq_b200.h."""
+    _fields_ = [("W", ctypes.c_void_p), ("P", ctypes.c_void_p), ("L", ctypes.c_void_p), ("err", ctypes.c_void_p),
+                ("wq", ctypes.c_void_p), ("enc", ctypes.c_void_p), ("size_k", ctypes.c_int64),
+                ("size_n", ctypes.c_int64), ("r0", ctypes.c_int64), ("end", ctypes.c_int64),
+                ("tile_col0", ctypes.c_int64), ("n_tiles", ctypes.c_int64)]
 
 _lib = None
 _lock = threading.Lock()
@@ -78,6 +89,7 @@ def load() -> ctypes.CDLL:
         L.kq_bf16_to_f32_transposed.argtypes = [P, I64, I64, I64, P, P, P]
         L.kq_gemm_abt_tf32.argtypes = [P, P, P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_float, P, P]
         L.kq_ldlq_step_encode.argtypes = [P, P, I64, I64, I64, I64, I, P, I, P, P, P, I, P, SZ, P]
+        L.kq_ldlq_chain_step.argtypes = [P, I, I, P, I, I, P, SZ, P]
         L.kq_hessian_workspace_bytes.argtypes = [I64, I64, I]
         L.kq_hessian_workspace_bytes.restype = SZ
         L.kq_accumulate_hessian.argtypes = [P, P, I64, I64, I64, P, I64, I, P, SZ, P, P]
@@ -408,4 +420,28 @@ def ldlq_step_encode(W: torch.Tensor, comp: torch.Tensor, r0: int, K: int, label
         if stats.timing:
             b.record()
             stats.events.append((a, b, B * (n // 16), int(tailbite_context)))
+    stats.launches += 1
+
+
+def ldlq_chain_step(items, K: int, labels: torch.Tensor, tailbite_context: int, device: torch.device,
+                    max_ctas: int = 0) -> None:
+    """One launch of LDLQ chain steps; ``items`` is a sequence of ChainItem (at most KQ_CHAIN_MAX_ITEMS)."""
+    n = len(items)
+    if not 1 <= n <= KQ_CHAIN_MAX_ITEMS:
+        raise ValueError(f"ldlq_chain_step: 1..{KQ_CHAIN_MAX_ITEMS} items")
+    arr = (ChainItem * n)(*items)
+    tiles = sum(int(it.n_tiles) for it in items)
+    with torch.cuda.device(device):
+        need = viterbi_workspace_bytes(K, tiles)
+        ws = workspace(device, need)
+        if stats.timing:
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+        _check(load().kq_ldlq_chain_step(ctypes.cast(arr, ctypes.c_void_p), n, int(K), labels.data_ptr(),
+                                         int(tailbite_context), int(max_ctas), ws.data_ptr(), ws.numel(),
+                                         _stream(device)), "kq_ldlq_chain_step")
+        if stats.timing:
+            b.record()
+            stats.events.append((a, b, tiles, int(tailbite_context)))
     stats.launches += 1

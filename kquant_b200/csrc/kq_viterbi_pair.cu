@@ -216,6 +216,7 @@ __device__ __forceinline__ void run_steps(
 //
 // FlatIO: tiles [n][256] already in trellis order, outputs alike.
 struct FlatIO {
+    static constexpr int kStageFloats = 0;
     const float* __restrict__ tiles;
     float* __restrict__ vals;
     uint16_t* __restrict__ states;
@@ -234,6 +235,7 @@ struct FlatIO {
 // W + comp, stores What = value, E = W - value and the state into
 // enc [b][r0 / 16][c][j].
 struct StepIO {
+    static constexpr int kStageFloats = 0;
     const float* __restrict__ W;
     const float* __restrict__ comp;    // [batch][16][n]
     float* __restrict__ wq;
@@ -265,6 +267,113 @@ struct StepIO {
     }
 };
 
+// ChainIO: tiles of up to KQ_CHAIN_MAX_ITEMS LDLQ chain items (see
+// kq_ldlq_chain_step); tile t belongs to the item whose [start, start + n)
+// range holds it.  The load computes the item's feedback for the element.
+struct ChainIO {
+    // Feedback rows staged per chunk: [tile of the pair][L | err][row][16].
+    static constexpr int kChunk = 112;
+    static constexpr int kStageFloats = 2 * 2 * kChunk * 16;
+    kq_chain_item it[KQ_CHAIN_MAX_ITEMS];
+    int64_t start[KQ_CHAIN_MAX_ITEMS + 1];
+    int n;
+    __device__ __forceinline__ int find(int64_t tile) const {
+        int i = 0;
+        while (i + 1 < n && tile >= start[i + 1]) ++i;
+        return i;
+    }
+    __device__ __forceinline__ void locate(const kq_chain_item& c, int64_t lt, int j, int64_t& R, int64_t& x,
+                                           int64_t& tc) const {
+        const int m = j >> 3, s = j & 7;
+        const int row = 2 * (m & 3) + (s & 1) + 8 * ((s >> 1) & 1);
+        const int col = (m >> 2) + 8 * (s >> 2);
+        tc = c.tile_col0 + lt;
+        R = c.r0 + row;
+        x = tc * 16 + col;
+    }
+    __device__ __forceinline__ float load(int64_t tile, int j) const {
+        const int i = find(tile);
+        const kq_chain_item& c = it[i];
+        int64_t R, x, tc;
+        locate(c, tile - start[i], j, R, x, tc);
+        const int64_t n = c.size_n, k = c.size_k;
+        float s = 0.f;
+        const float* lp = c.L + (c.r0 + 16) * k + R;
+        const float* ep = c.err + (c.r0 + 16) * n + x;
+#pragma unroll 8
+        for (int64_t q = c.r0 + 16; q < c.end; ++q) {
+            s = fmaf(__ldg(lp), __ldcg(ep), s);
+            lp += k;
+            ep += n;
+        }
+        const float comp = c.P[R * n + x] + s;
+        return c.W[R * n + x] + comp;
+    }
+    // Element j of tile (2q + t) for every thread of the CTA (t = tid / 256,
+    // j = tid % 256), both tiles of the pair at once: the feedback rows of
+    // each tile (L[r0+16+i][r0..r0+15], err[r0+16+i][16 tile columns]) go to
+    // shared memory in chunks of kChunk rows with coalesced 16-byte loads,
+    // then each thread sums its element's row in ascending order (the same
+    // fp32 fma chain as load()).  Called by all threads; contains barriers.
+    __device__ __forceinline__ float load_staged(int64_t tA, int64_t tB, int t, int j, float* stage,
+                                                 int tid) const {
+        const int iA = find(tA), iB = find(tB);
+        const kq_chain_item& cA = it[iA];
+        const kq_chain_item& cB = it[iB];
+        const int64_t mA = cA.end - cA.r0 - 16, mB = cB.end - cB.r0 - 16;
+        const int64_t tcA = cA.tile_col0 + (tA - start[iA]), tcB = cB.tile_col0 + (tB - start[iB]);
+        const kq_chain_item& c = t ? cB : cA;
+        int64_t R, x, tc;
+        locate(c, (t ? tB : tA) - start[t ? iB : iA], j, R, x, tc);
+        const int row = (int)(R - c.r0), col = (int)(x - tc * 16);
+        const int64_t m = t ? mB : mA;
+        const int64_t mmax = mA > mB ? mA : mB;
+        float s = 0.f;
+        for (int64_t c0 = 0; c0 < mmax; c0 += kChunk) {
+            for (int idx = tid; idx < 2 * 2 * kChunk * 4; idx += kThreads) {
+                const int tt = idx / (2 * kChunk * 4);
+                const int rem = idx - tt * (2 * kChunk * 4);
+                const int which = rem / (kChunk * 4);
+                const int i = (rem >> 2) % kChunk, quad = rem & 3;
+                const kq_chain_item& ci = tt ? cB : cA;
+                const int64_t mi = tt ? mB : mA;
+                if (c0 + i < mi) {
+                    const int64_t q = ci.r0 + 16 + c0 + i;
+                    const float4 v = which == 0
+                        ? __ldg(reinterpret_cast<const float4*>(ci.L + q * ci.size_k + ci.r0) + quad)
+                        : __ldcg(reinterpret_cast<const float4*>(ci.err + q * ci.size_n + (tt ? tcB : tcA) * 16) + quad);
+                    reinterpret_cast<float4*>(stage + ((tt * 2 + which) * kChunk + i) * 16)[quad] = v;
+                }
+            }
+            __syncthreads();
+            const float* ls = stage + (t * 2 + 0) * kChunk * 16 + row;
+            const float* es = stage + (t * 2 + 1) * kChunk * 16 + col;
+            const int cnt = (int)((m - c0) < kChunk ? (m - c0) : kChunk);
+            for (int i = 0; i < cnt; ++i) s = fmaf(ls[i * 16], es[i * 16], s);
+            __syncthreads();
+        }
+        const int64_t n = c.size_n;
+        const float comp = __ldcg(c.P + R * n + x) + s;
+        return __ldg(c.W + R * n + x) + comp;
+    }
+    __device__ __forceinline__ void store(int64_t tile, int j, uint16_t sv, float v) const {
+        const int i = find(tile);
+        const kq_chain_item& c = it[i];
+        int64_t R, x, tc;
+        locate(c, tile - start[i], j, R, x, tc);
+        const int64_t n = c.size_n;
+        c.wq[R * n + x] = v;
+        c.err[R * n + x] = c.W[R * n + x] - v;
+        c.enc[(((c.r0 >> 4) * (n >> 4)) + tc) * 256 + j] = sv;
+    }
+};
+
+template <int K>
+__host__ __device__ constexpr size_t pair_smem_bytes() {
+    return (size_t)2 * PairMap<K>::NODES * 4 + kJobs * 256 * 4 + kJobs * 2 * 256 * 2 + kJobs * 2 * 16 * 4 +
+           kJobs * 2 * 4;
+}
+
 template <int K, class IO>
 __global__ void __launch_bounds__(kThreads, 1)
 pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
@@ -279,6 +388,7 @@ pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
     uint16_t* enc = reinterpret_cast<uint16_t*>(wsh + kJobs * 256);     // [kJobs][2][256]
     uint32_t* red = reinterpret_cast<uint32_t*>(enc + kJobs * 2 * 256); // [kJobs][2][16]
     int* es_sh = reinterpret_cast<int*>(red + kJobs * 2 * 16);          // [kJobs][2]
+    float* stage = reinterpret_cast<float*>(smem + ((pair_smem_bytes<K>() + 15) & ~(size_t)15));   // IO staging
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -304,7 +414,14 @@ pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
         const int t = tid >> 8, r = tid & 255;
         int64_t tile = 2 * q + t;
         if (tile >= n_tiles) tile = 2 * q;
-        reinterpret_cast<__half*>(wsh + j * 256 + r)[t] = __float2half_rn(io.load(tile, r));
+        float v;
+        if constexpr (IO::kStageFloats > 0) {
+            const int64_t tB = (2 * q + 1 < n_tiles) ? 2 * q + 1 : 2 * q;
+            v = io.load_staged(2 * q, tB, t, r, stage, tid);
+        } else {
+            v = io.load(tile, r);
+        }
+        reinterpret_cast<__half*>(wsh + j * 256 + r)[t] = __float2half_rn(v);
     };
 
     int phase[kJobs], step[kJobs], par[kJobs];
@@ -538,11 +655,6 @@ pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
     }
 }
 
-template <int K>
-constexpr size_t pair_smem_bytes() {
-    return (size_t)2 * PairMap<K>::NODES * 4 + kJobs * 256 * 4 + kJobs * 2 * 256 * 2 + kJobs * 2 * 16 * 4 +
-           kJobs * 2 * 4;
-}
 
 template <int K>
 void pair_grid(int64_t n, int sms, int& grid, int& njobs) {
@@ -554,7 +666,7 @@ void pair_grid(int64_t n, int sms, int& grid, int& njobs) {
 template <int K, class IO>
 int pair_run(const IO& io, int64_t n, const uint16_t* labels, int C, int grid, int njobs, uint8_t* dec,
              cudaStream_t stream) {
-    const size_t sm = pair_smem_bytes<K>();
+    const size_t sm = ((pair_smem_bytes<K>() + 15) & ~(size_t)15) + (size_t)IO::kStageFloats * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(pair_kernel<K, IO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
     pair_kernel<K, IO><<<grid, kThreads, sm, stream>>>(io, n, reinterpret_cast<const uint32_t*>(labels),
@@ -615,8 +727,8 @@ static int pair_launch_bounded(const float* tiles, int64_t n, const uint16_t* la
 }
 
 // One LDLQ step (StepIO) through the same kernel and grid policy as pair_launch.
-template <int K>
-int step_launch(const StepIO& io, int64_t n, const uint16_t* labels, int C, int max_ctas, uint8_t* ws,
+template <int K, class IO>
+int step_launch(const IO& io, int64_t n, const uint16_t* labels, int C, int max_ctas, uint8_t* ws,
                 size_t ws_bytes, cudaStream_t stream) {
     int sms = 0;
     if (int rc = sm_count(&sms)) return rc;
@@ -631,12 +743,13 @@ int step_launch(const StepIO& io, int64_t n, const uint16_t* labels, int C, int 
     return pair_run<K>(io, n, labels, C, grid, njobs, ws, stream);
 }
 
-int ldlq_step_encode(const StepIO& io, int64_t n, int K, const uint16_t* labels, int C, int max_ctas, uint8_t* ws,
+template <class IO>
+int ldlq_step_encode(const IO& io, int64_t n, int K, const uint16_t* labels, int C, int max_ctas, uint8_t* ws,
                      size_t ws_bytes, cudaStream_t stream) {
     switch (K) {
-    case 2: return step_launch<2>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
-    case 3: return step_launch<3>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
-    case 4: return step_launch<4>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
+    case 2: return step_launch<2, IO>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
+    case 3: return step_launch<3, IO>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
+    case 4: return step_launch<4, IO>(io, n, labels, C, max_ctas, ws, ws_bytes, stream);
     default: set_error("viterbi: K must be 2, 3 or 4 (got %d)", K); return KQ_ERR_ARG;
     }
 }
@@ -676,5 +789,47 @@ extern "C" int kq_ldlq_step_encode(const float* W, const float* comp, int64_t ba
     if (size_n / 16 > 0x7FFFFFFF) { set_error("kq_ldlq_step_encode: n too large"); return KQ_ERR_ARG; }
     StepIO io{W, comp, wq, err, enc, size_k, size_n, r0, (int)(size_n / 16)};
     return ldlq_step_encode(io, batch * (size_n / 16), K, labels, tailbite_ctx, max_ctas, static_cast<uint8_t*>(workspace),
+                            workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int K, const uint16_t* labels,
+                                  int tailbite_ctx, int max_ctas, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+    using namespace kq;
+    if (!items || n_items < 1 || n_items > KQ_CHAIN_MAX_ITEMS || !labels) {
+        set_error("kq_ldlq_chain_step: need 1..%d items and labels (got %d)", KQ_CHAIN_MAX_ITEMS, n_items);
+        return KQ_ERR_ARG;
+    }
+    if (tailbite_ctx < 1 || tailbite_ctx > 128) {
+        set_error("tailbite_context must be in 1..128 (got %d)", tailbite_ctx);
+        return KQ_ERR_ARG;
+    }
+    if (((uintptr_t)labels & 3) || ((uintptr_t)workspace & 15)) {
+        set_error("kq_ldlq_chain_step: labels must be 4-byte and workspace 16-byte aligned");
+        return KQ_ERR_ALIGN;
+    }
+    ChainIO io;
+    io.n = n_items;
+    int64_t total = 0;
+    for (int i = 0; i < n_items; ++i) {
+        const kq_chain_item& c = items[i];
+        if (!c.W || !c.P || !c.L || !c.err || !c.wq || !c.enc) {
+            set_error("kq_ldlq_chain_step: item %d has a null pointer", i);
+            return KQ_ERR_ARG;
+        }
+        if (c.size_k <= 0 || c.size_n <= 0 || c.size_k % 16 || c.size_n % 16 || c.r0 < 0 || c.r0 % 16 ||
+            c.end < c.r0 + 16 || c.end > c.size_k || c.n_tiles <= 0 || c.tile_col0 < 0 ||
+            c.tile_col0 + c.n_tiles > c.size_n / 16) {
+            set_error("kq_ldlq_chain_step: item %d has a bad shape (k=%lld n=%lld r0=%lld end=%lld tiles %lld+%lld)",
+                      i, (long long)c.size_k, (long long)c.size_n, (long long)c.r0, (long long)c.end,
+                      (long long)c.tile_col0, (long long)c.n_tiles);
+            return KQ_ERR_ARG;
+        }
+        io.it[i] = c;
+        io.start[i] = total;
+        total += c.n_tiles;
+    }
+    io.start[n_items] = total;
+    return ldlq_step_encode(io, total, K, labels, tailbite_ctx, max_ctas, static_cast<uint8_t*>(workspace),
                             workspace_bytes, static_cast<cudaStream_t>(stream));
 }

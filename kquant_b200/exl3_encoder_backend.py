@@ -519,13 +519,12 @@ def _ldlq_traverse(weights, Ls, quant_args, plan: _RatePlan, **kw):
 
 def _ldlq_traverse_steps(weights, Ls, quant_args, plan: _RatePlan, *, buffer_rows: int, tf32: bool,
                          process_begin: int = 0, process_end: int | None = None, state=None,
-                         source_indices: torch.Tensor | None = None, pb=None, launch_ctl: dict | None = None):
+                         source_indices: torch.Tensor | None = None, pb=None):
     """Backward block-LDLQ over rows [process_begin, process_end) of a batch.
 
     A generator: it yields after enqueueing each 16-row step (so several
     independent traversals can be interleaved on their own streams) and
-    returns (What, enc, P).  ``launch_ctl["max_ctas"]``, read at every step,
-    caps the grid of the fused step's Viterbi launch.
+    returns (What, enc, P).
 
     weights [S, k, n] and Ls [S, k, k] are sources; members read source
     ``source_indices[b]`` (identity when None).  For every 16-row step
@@ -580,8 +579,7 @@ def _ldlq_traverse_steps(weights, Ls, quant_args, plan: _RatePlan, *, buffer_row
                 r0 = begin + local_end - 16
                 r1 = r0 + 16
                 comp = _baddbmm_ldlq(P[:, r0:r1], Ls[:, r1:end, r0:r1].transpose(1, 2), E[:, r1:end], tf32=tf32)
-                _native.ldlq_step_encode(weights, comp.contiguous(), r0, bits, labels, ctx, wq, E, enc,
-                                         max_ctas=launch_ctl.get("max_ctas", 0) if launch_ctl else 0)
+                _native.ldlq_step_encode(weights, comp.contiguous(), r0, bits, labels, ctx, wq, E, enc)
                 if pb:
                     progress += 1
                     pb.update(progress)
@@ -1565,14 +1563,15 @@ def _uniform_prepare(weights: list[torch.Tensor], H_datas: list[dict], quant_arg
     return state
 
 
-def _uniform_traversal(state: dict, launch_ctl: dict | None = None):
-    """Phase 2: the LDLQ traversal of a prepared batch, as a step generator returning (What, enc)."""
+def _uniform_members(state: dict):
+    """Chain-engine members of a prepared batch: one per stacked matrix; returns (members, What, enc)."""
     W, Ls = state["ldlq"]
     qa0 = state["quant_args_list"][0]
-    plan = _RatePlan(int(qa0["K"]), None, W.shape[0], W.shape[2] // 16, W.device)
-    wq, enc, _ = yield from _ldlq_traverse_steps(W, Ls, qa0, plan, buffer_rows=_buffer_rows(qa0, W.shape[1]),
-                                                 tf32=bool(qa0.get("ldlq_tf32", False)), launch_ctl=launch_ctl)
-    return wq, enc
+    B, size_k, size_n = W.shape
+    wq = torch.empty_like(W)
+    enc = torch.empty((B, size_k // 16, size_n // 16, 256), dtype=torch.int16, device=W.device)
+    members = [_ChainMember(W[b], Ls[b if Ls.shape[0] == B else 0], wq[b], enc[b], qa0) for b in range(B)]
+    return members, wq, enc
 
 
 def _uniform_finish(state: dict, wq: torch.Tensor, enc: torch.Tensor):
@@ -1643,28 +1642,35 @@ def quantize_uniform_batch(weights: list[torch.Tensor], H_datas: list[dict], qua
     devices = quant_args_list[0]["devices"]
     _sync(devices)
     with torch.cuda.stream(get_quant_stream(state["device"])):
-        wq, enc = _drive(_uniform_traversal(state))
+        if len(devices) == 1:
+            members, wq, enc = _uniform_members(state)
+            _chain_traverse(members, state["device"])
+        else:
+            wq, enc = _uniform_traversal_multigpu(state)
     _sync(devices)
     return _uniform_finish(state, wq, enc)
 
 
+def _uniform_traversal_multigpu(state: dict):
+    """Uniform-batch traversal whose tile launches split across several devices (quantize_tiles_multigpu)."""
+    W, Ls = state["ldlq"]
+    qa0 = state["quant_args_list"][0]
+    plan = _RatePlan(int(qa0["K"]), None, W.shape[0], W.shape[2] // 16, W.device)
+    wq, enc, _ = _ldlq_traverse(W, Ls, qa0, plan, buffer_rows=_buffer_rows(qa0, W.shape[1]),
+                                tf32=bool(qa0.get("ldlq_tf32", False)))
+    return wq, enc
+
+
 def quantize_uniform_batches(groups, verbose: bool = False):
-    """Several independent ``quantize_uniform_batch`` calls with overlapped LDLQ traversals.
+    """Several independent ``quantize_uniform_batch`` calls whose LDLQ traversals share launches.
 
-    ``groups`` is a list of (weights, H_datas, quant_args_list).  Results
-    equal the sequential calls bit for bit (same RNG seeding, same
-    arithmetic, same launches): the preparation phases run in order, then
-    the traversals advance step by step on their own CUDA streams, then the
-    outputs are built in order.  Returns one result list per group.
-
-    Schedule.  A Viterbi launch of n tiles runs in ceil(n / (2 SMs)) waves of
-    one tile pair per SM, so a step of n <= 2 SMs tiles leaves
-    SMs - ceil(n / 2) SMs idle for its whole duration.  The primary
-    traversal (longest critical path among those that fit one wave) runs on
-    a high-priority stream with full grids; the others run one after another
-    on a low-priority stream with their grid capped at the primary's idle
-    SMs for the steps predicted to overlap it, and with full grids after
-    that.  Groups spanning several devices, or with no idle SMs to fill, run
+    ``groups`` is a list of (weights, H_datas, quant_args_list).  The
+    preparation phases run in order (same RNG seeding as sequential calls),
+    then every matrix of every group is one set of chains in a single
+    chain-engine run (:func:`_chain_traverse`), then the outputs are built in
+    order.  Results equal the sequential calls bit for bit: a chain step's
+    arithmetic does not depend on which other chains share its launch.
+    Returns one result list per group.  Groups spanning several devices run
     sequentially.
     """
     groups = [(list(w), list(h), list(q)) for w, h, q in groups]
@@ -1673,100 +1679,138 @@ def quantize_uniform_batches(groups, verbose: bool = False):
     states = [_uniform_prepare(w, h, q, verbose) for w, h, q in groups]
     live = [i for i, st in enumerate(states) if st["ldlq"] is not None]
     out = {}
-    if live:
-        dev = states[live[0]]["device"]
-        sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        shape = {i: states[i]["ldlq"][0].shape for i in live}
-        tiles = {i: shape[i][0] * shape[i][2] // 16 for i in live}
-        steps = {i: shape[i][1] // 16 for i in live}
-        one_wave = [i for i in live if tiles[i] <= 2 * sms]
-        primary = max(one_wave, key=lambda i: steps[i]) if one_wave else None
-        spare = sms - (tiles[primary] + 1) // 2 if primary is not None else 0
-        if (primary is None or spare < 4 or len(live) < 2
-                or any(str(states[i]["device"]) != str(dev) for i in live)):
-            for i in live:
-                _sync(states[i]["quant_args_list"][0]["devices"])
-                with torch.cuda.stream(get_quant_stream(states[i]["device"])):
-                    out[i] = _drive(_uniform_traversal(states[i]))
-        else:
-            out = _overlap_traversals(states, live, primary, steps, tiles, sms, spare, dev)
-    results = []
-    for i, st in enumerate(states):
-        results.append(st["results"] if st["ldlq"] is None else _uniform_finish(st, *out[i]))
-    return results
+    by_device: dict = {}
+    for i in live:
+        by_device.setdefault(str(states[i]["device"]), []).append(i)
+    for dev_name, idx in by_device.items():
+        dev = torch.device(dev_name)
+        _sync([dev_name])
+        with torch.cuda.stream(get_quant_stream(dev)):
+            members = []
+            for i in idx:
+                m, wq, enc = _uniform_members(states[i])
+                members += m
+                out[i] = (wq, enc)
+            _chain_traverse(members, dev)
+        _sync([dev_name])
+    return [st["results"] if st["ldlq"] is None else _uniform_finish(st, *out[i]) for i, st in enumerate(states)]
 
 
-@lru_cache
-def _overlap_streams(device):
-    """(high, low) priority streams of a device, created once so the caching
-    allocator's per-stream pools are reused from call to call."""
-    return torch.cuda.Stream(device=device, priority=-1), torch.cuda.Stream(device=device, priority=0)
+# --------------------------------------------------------------------------
+# LDLQ chain engine
+# --------------------------------------------------------------------------
+
+# Tile columns per chain.  Columns of a matrix are independent under LDLQ
+# (the feedback of column j reads only column j of the error rows), so a
+# matrix splits into chains that may sit at different rows.  Narrow chains
+# let a launch be filled to whole waves of 2 x SMs tiles.
+CHAIN_TILES = 32
 
 
-# Fraction of the primary's predicted duration that capped secondary steps
-# may fill; the margin absorbs prediction error (a capped step left over
-# after the primary ends would run alone on a few SMs).
-OVERLAP_BUDGET = 1.0
+class _ChainMember:
+    """One [k, n] matrix of a chain-engine run with its LDLQ state."""
+
+    def __init__(self, W, L, wq, enc, quant_args):
+        self.W = W
+        self.L = L.contiguous()
+        self.wq = wq
+        self.enc = enc
+        self.k, self.n = W.shape
+        assert W.is_contiguous() and wq.is_contiguous() and enc.is_contiguous()
+        assert self.k % 16 == 0 and self.n % 16 == 0
+        self.P = torch.zeros_like(W)
+        self.E = torch.empty_like(W)
+        self.buffer_rows = _buffer_rows(quant_args, self.k)
+        self.tf32 = bool(quant_args.get("ldlq_tf32", False))
+        bits = int(quant_args["K"])
+        if bits not in (2, 3, 4):
+            raise ValueError("the trellis kernel supports K2--K4")
+        ctx = int(quant_args.get("tailbite_context", 128))
+        if not 1 <= ctx <= 128:
+            raise ValueError("tailbite_context must be in 1..128")
+        kind, lut = _tile_codebook(quant_args, bits)
+        self.labels = _labels_for(W.device, bits, kind, lut)
+        self.key = (bits, self.labels.data_ptr(), ctx)
 
 
-def _overlap_traversals(states, live, primary, steps, tiles, sms, spare, dev):
-    """Drive the traversals of quantize_uniform_batches; returns {group: (What, enc)}.
+class _Chain:
+    def __init__(self, member: _ChainMember, tile_col0: int, n_tiles: int):
+        self.m = member
+        self.tile_col0 = tile_col0
+        self.n_tiles = n_tiles
+        rows = member.buffer_rows
+        # (r0, end) of every step, in traversal order (backward over 128-row buffers)
+        self.steps = [(end - rows + le - 16, end) for end in range(member.k, 0, -rows)
+                      for le in range(rows, 0, -16)]
+        self.pos = 0
 
-    1. Primary steps (high priority, full grid) and capped secondary steps (low
-       priority, grid = the primary's idle SMs) are enqueued in order of their
-       predicted finish, until the capped budget is used.
-    2. The remaining primary steps are enqueued and their end is recorded.
-    3. The low stream waits for that event, then runs the remaining
-       secondary steps with full grids, so they never compete with the primary.
-    """
-    _sync([str(dev)])
-    hi, lo = _overlap_streams(dev)
-    start = torch.cuda.current_stream(dev).record_event()
-    hi.wait_event(start)
-    lo.wait_event(start)
-    out = {}
+    @property
+    def remaining(self):
+        return len(self.steps) - self.pos
 
-    def advance(i, gen, stream):
-        with torch.cuda.device(dev), torch.cuda.stream(stream):
+    def item(self):
+        m = self.m
+        r0, end = self.steps[self.pos]
+        return _native.ChainItem(m.W.data_ptr(), m.P.data_ptr(), m.L.data_ptr(), m.E.data_ptr(), m.wq.data_ptr(),
+                                 m.enc.data_ptr(), m.k, m.n, r0, end, self.tile_col0, self.n_tiles)
+
+    def advance(self):
+        """Step done: after a buffer's last step, P[:begin] += L[begin:end, :begin]^T E[begin:end] (own columns)."""
+        r0, end = self.steps[self.pos]
+        self.pos += 1
+        begin = end - self.m.buffer_rows
+        if r0 == begin and begin > 0:
+            m = self.m
+            c0, c1 = 16 * self.tile_col0, 16 * (self.tile_col0 + self.n_tiles)
+            previous = torch.backends.cuda.matmul.allow_tf32
+            torch.backends.cuda.matmul.allow_tf32 = m.tf32
             try:
-                next(gen)
-                return True
-            except StopIteration as fin:
-                out[i] = fin.value
-                return False
+                m.P[:begin, c0:c1].addmm_(m.L[begin:end, :begin].T, m.E[begin:end, c0:c1])
+            finally:
+                torch.backends.cuda.matmul.allow_tf32 = previous
 
-    ctl = {"max_ctas": spare}
-    queue = [i for i in live if i != primary]
-    gens = {i: _uniform_traversal(states[i], ctl) for i in queue}
-    prim = _uniform_traversal(states[primary])
-    budget = OVERLAP_BUDGET * steps[primary]
-    t_hi = t_lo = 0.0
-    prim_live = True
-    while queue and prim_live:
-        cur = queue[0]
-        cost = -(-((tiles[cur] + 1) // 2) // spare)         # pair-rounds of one capped step
-        if t_lo + cost > budget:
-            break
-        if t_hi <= t_lo:
-            prim_live = advance(primary, prim, hi)
-            t_hi += 1
-        else:
-            if advance(cur, gens[cur], lo):
-                t_lo += cost
-            else:
-                queue.pop(0)
-    while prim_live:
-        prim_live = advance(primary, prim, hi)
-    lo.wait_event(hi.record_event())
-    ctl["max_ctas"] = 0
-    for i in queue:
-        while advance(i, gens[i], lo):
-            pass
-    cur_stream = torch.cuda.current_stream(dev)
-    cur_stream.wait_stream(hi)
-    cur_stream.wait_stream(lo)
-    _sync([str(dev)])
-    return out
+
+def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None = None) -> None:
+    """Block-LDLQ of every member (kquant/exl3_encoder_backend.py:389-505 per matrix), fills What and codes.
+
+    Each member splits into column chains of ``CHAIN_TILES`` tiles.  Every
+    launch (``kq_ldlq_chain_step``) advances a set of chains by one 16-row
+    step: the chains with the most steps left first (the critical path),
+    then any others that fit the launch's whole waves of 2 x SMs tiles,
+    all with the same (K, codebook, context).  The kernel computes each
+    step's feedback product itself; the buffer-end feedback updates run
+    between launches on the same stream.
+    """
+    width = chain_tiles or CHAIN_TILES
+    chains = []
+    for m in members:
+        tn = m.n // 16
+        for c0 in range(0, tn, width):
+            chains.append(_Chain(m, c0, min(width, tn - c0)))
+    cap = 2 * torch.cuda.get_device_properties(device).multi_processor_count
+    order = {id(c): i for i, c in enumerate(chains)}
+    live = list(chains)
+    while live:
+        live.sort(key=lambda c: (-c.remaining, order[id(c)]))
+        key = live[0].m.key
+        cand = [c for c in live if c.m.key == key]
+        sel, tot = [], 0
+        for c in cand:
+            if len(sel) < _native.KQ_CHAIN_MAX_ITEMS and (tot + c.n_tiles <= cap or not sel):
+                sel.append(c)
+                tot += c.n_tiles
+        waves = -(-tot // cap)
+        for c in cand:
+            if c in sel or len(sel) >= _native.KQ_CHAIN_MAX_ITEMS:
+                continue
+            if tot + c.n_tiles <= waves * cap:
+                sel.append(c)
+                tot += c.n_tiles
+        bits, _, ctx = key
+        _native.ldlq_chain_step([c.item() for c in sel], bits, sel[0].m.labels, ctx, device)
+        for c in sel:
+            c.advance()
+        live = [c for c in live if c.remaining > 0]
 
 
 def pack_signs(signs: torch.Tensor, quant_args: dict) -> torch.Tensor:

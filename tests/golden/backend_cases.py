@@ -21,3 +21,17 @@ def make_inputs(case, device):
             "devices": [str(device)], "apply_out_scales": None, "tailbite_context": case["ctx"],
             "sqg_e4m3_luts_by_bits": {b: sqg_xor_cheb_t12_bytes(b) for b in (2, 3, 4)}}
     return w.to(device), h.to(device), args
+
+
+# quantize_uniform_batch fixture: two matrices sharing one H (gate/up style)
+UNIFORM_CASES = {
+    "uniform_pair_k3": {"k": 256, "n": 256, "K": 3, "ctx": 128, "seed": 13},
+}
+
+
+def make_uniform_inputs(case, device):
+    w1, h, a1 = make_inputs(case, device)
+    w2, _, _ = make_inputs(dict(case, seed=case["seed"] + 100), device)
+    a2 = dict(a1, sv_seed=a1["sv_seed"] + 1)
+    a2["sqg_e4m3_luts_by_bits"] = a1["sqg_e4m3_luts_by_bits"]
+    return [w1, w2], h, [a1, a2]

@@ -10,7 +10,8 @@ Viterbi kernel, pinned against it bit for bit on the GPU).  Random sign draws
 use the CPU generator; the GPU test reproduces them the same way.
 
 Usage: python tests/golden/make_backend_fixtures.py /path/to/reference
-Writes tests/golden/backend_<case>.npz.
+Writes tests/golden/backend_<case>.npz (quantize_qsrt cases and the
+quantize_uniform_batch cases).
 """
 from __future__ import annotations
 
@@ -27,7 +28,7 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
 
-from tests.golden.backend_cases import CASES, make_inputs  # noqa: E402
+from tests.golden.backend_cases import CASES, UNIFORM_CASES, make_inputs, make_uniform_inputs  # noqa: E402
 
 
 def _load_reference_backend(ref_root: Path):
@@ -98,6 +99,19 @@ def main():
             trellis=out["trellis"].numpy(), g_scale=np.array(args["g_scale"]),
             states=unpack_trellis_states(out["trellis"], args["K"]).numpy())
         print(name, "proxy", proxy, "g_scale", args["g_scale"])
+    for name, case in UNIFORM_CASES.items():
+        ws, h, args = make_uniform_inputs(case, "cpu")
+        from kquant.ldlq import make_shared_h
+        from kquant.qsrt import unpack_trellis_states
+        shared = make_shared_h(ws[0].shape[0], torch.device("cpu"), h)
+        res = be.quantize_uniform_batch([w.clone() for w in ws], [shared, shared], args)
+        fields = {}
+        for t, (proxy, out) in enumerate(res):
+            fields.update({f"proxy{t}": np.array(proxy), f"suh{t}": out["suh"].numpy(), f"svh{t}": out["svh"].numpy(),
+                           f"g_scale{t}": np.array(args[t]["g_scale"]),
+                           f"states{t}": unpack_trellis_states(out["trellis"], args[t]["K"]).numpy()})
+            print(name, t, "proxy", proxy, "g_scale", args[t]["g_scale"])
+        np.savez_compressed(HERE / f"backend_{name}.npz", **fields)
 
 
 if __name__ == "__main__":

@@ -18,7 +18,7 @@ import torch
 
 from kquant_b200 import exl3_encoder_backend as be
 from kquant_b200.ldlq import make_shared_h
-from tests.golden.backend_cases import CASES, make_inputs
+from tests.golden.backend_cases import CASES, UNIFORM_CASES, make_inputs, make_uniform_inputs
 
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -60,3 +60,29 @@ def test_backend_matches_reference_fixture(cuda_device, cpu_sign_draws, name):
         # identical rotated inputs: codes bit-exact and reconstruction within 1e-3
         assert stats["states_equal"] == 1.0
         assert stats["recon_maxabs"] < 1e-3
+
+
+@pytest.mark.parametrize("name", sorted(UNIFORM_CASES))
+def test_uniform_batch_matches_reference_fixture(cuda_device, cpu_sign_draws, name):
+    """quantize_uniform_batch (the LDLQ chain engine) against the reference's quantize_uniform_batch."""
+    ref = np.load(GOLDEN / f"backend_{name}.npz")
+    ws, h, args = make_uniform_inputs(UNIFORM_CASES[name], cuda_device)
+    shared = make_shared_h(ws[0].shape[0], cuda_device, h)
+    res = be.quantize_uniform_batch([w.clone() for w in ws], [shared, shared], args)
+    torch.cuda.synchronize()
+    for t, (proxy, out) in enumerate(res):
+        ref_proxy = float(ref[f"proxy{t}"])
+        states = be._native.unpack_trellis_states(out["trellis"], args[t]["K"]).cpu().numpy()
+        stats = {
+            "proxy_rel": abs(proxy - ref_proxy) / ref_proxy,
+            "g_scale_rel": abs(args[t]["g_scale"] - float(ref[f"g_scale{t}"])) / float(ref[f"g_scale{t}"]),
+            "suh_equal": float((out["suh"].cpu().numpy() == ref[f"suh{t}"]).mean()),
+            "svh_equal": float((out["svh"].cpu().numpy() == ref[f"svh{t}"]).mean()),
+            "states_equal": float((states == ref[f"states{t}"]).mean()),
+        }
+        print(name, t, json.dumps(stats))
+        assert stats["proxy_rel"] < 0.01
+        assert stats["g_scale_rel"] < 1e-3
+        assert stats["suh_equal"] > 0.99 and stats["svh_equal"] > 0.99
+        if stats["suh_equal"] == 1.0 and stats["svh_equal"] == 1.0:
+            assert stats["states_equal"] == 1.0
