@@ -512,8 +512,8 @@ def main():
                      "frac": (achieved_ops / peak_ops) if achieved_ops else None,
                      "traffic": traffic, "launches": vl, "avg_launch_ms": vsum / vl * 1e3 if vl else None,
                      "busy_ms": vsec * 1e3,
-                     "timing": "achieved = relaxations / union of the launch intervals (two LDLQ traversals "
-                               "overlap on two streams)",
+                     "timing": "achieved = relaxations / union of the Viterbi launch intervals (CUDA events "
+                               "on the launching stream)",
                      "peak_source": "measured HFMA2 rate (kq_probe_hfma2) x 2 lanes, this GPU, this run"},
         "viterbi_share_of_step": vsec / elapsed if elapsed else None,
         "clocks": clocks,
