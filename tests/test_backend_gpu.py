@@ -161,3 +161,29 @@ def test_fused_ldlq_step_equals_unfused(cuda_device, B, k, n):
     assert torch.equal(fused[0], plain[0])
     assert torch.equal(fused[1], plain[1])
     assert torch.equal(fused[2], plain[2])
+
+
+def test_chain_engine_long_buffers_and_stacked_members(cuda_device):
+    """Chain engine with 256-row LDLQ buffers (feedback staged in two chunks) and distinct-H members:
+    closed trellises, sane proxies, and uniform_batches == sequential uniform_batch."""
+    dev = cuda_device
+    w1, h1 = _problem(dev, k=512, n=256, seed=31)
+    w2, h2 = _problem(dev, k=512, n=256, seed=32)
+    w3, h3 = _problem(dev, k=256, n=384, seed=33)
+
+    def groups():
+        return [([w1.clone(), w2.clone()], [make_shared_h(512, dev, h1), make_shared_h(512, dev, h2)],
+                 [_args(dev, seed=1, sv_seed=2, buf_size_k=256), _args(dev, seed=1, sv_seed=3, buf_size_k=256)]),
+                ([w3.clone()], [make_shared_h(256, dev, h3)], [_args(dev, seed=4, sv_seed=5, K=4)])]
+
+    seq = [be.quantize_uniform_batch(w, h, q) for w, h, q in groups()]
+    conc = be.quantize_uniform_batches(groups())
+    for rs, rc in zip(seq, conc):
+        for (ps, os_), (pc, oc) in zip(rs, rc):
+            assert 0 < ps < 0.2 and ps == pc
+            assert torch.equal(os_["trellis"], oc["trellis"])
+    for res, K in ((seq[0], 3), (seq[1], 4)):
+        for _, out in res:
+            st = _native.unpack_trellis_states(out["trellis"], K).view(-1, 256).long() & 0xFFFF
+            prev = torch.roll(st, 1, dims=1)
+            assert torch.equal(((prev << K) | (st & ((1 << K) - 1))) & 0xFFFF, st)
