@@ -46,6 +46,16 @@ CONFIG = {"workload": "kimi_expert_triplet_k3", "matrices": "gate,up [7168x2048]
           "l2": "inputs larger than L2 (bf16 weights 88 MB + H 222 MB per step)"}
 
 
+def _set_rate(K: int) -> None:
+    """Run the triplet at another rate (BASELINE's metric is quoted at 2/3/4 bpw; configs[1] is K=3)."""
+    global K_BITS, METRIC, CONFIG
+    if K not in (2, 3, 4):
+        raise SystemExit("the trellis kernel supports K2--K4")
+    K_BITS = K
+    METRIC = f"EXL3 encoded Mweights/s (K={K}, expert triplet)"
+    CONFIG = dict(CONFIG, K=K, workload=f"kimi_expert_triplet_k{K}")
+
+
 def _dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -57,19 +67,24 @@ def _dist():
     return world, rank, local
 
 
-def make_triplet(device: torch.device, seed: int):
-    """Synthetic bf16 expert weights (HF orientation) and the two fp32 Hessians."""
+def make_triplet_weights(device: torch.device, seed: int):
+    """Synthetic bf16 expert weights (HF orientation): N(0, 0.015^2) entries, rows scaled by |Student-t(4)|
+    normalised to unit median.  Returns ((gate, up, down), the generator to continue from, None)."""
     g = torch.Generator(device=device).manual_seed(seed)
 
     def weight(rows, cols):
-        # N(0, 0.015^2) entries, rows scaled by |Student-t(4)| normalised to unit median
         w = torch.randn((rows, cols), generator=g, device=device) * 0.015
         z = torch.randn((rows, 5), generator=g, device=device)
         t = z[:, 0] / torch.sqrt((z[:, 1:] ** 2).sum(1) / 4)
         s = t.abs() / t.abs().median()
         return (w * s.unsqueeze(1)).to(torch.bfloat16)
 
-    gate, up, down = weight(INTER, HIDDEN), weight(INTER, HIDDEN), weight(HIDDEN, INTER)
+    return (weight(INTER, HIDDEN), weight(INTER, HIDDEN), weight(HIDDEN, INTER)), g, None
+
+
+def make_triplet(device: torch.device, seed: int):
+    """Synthetic bf16 expert weights (HF orientation) and the two fp32 Hessians."""
+    (gate, up, down), g, _ = make_triplet_weights(device, seed)
     chan = torch.exp(torch.randn(HIDDEN, generator=g, device=device))
     x = torch.randn((TOKENS, HIDDEN), generator=g, device=device) * chan
     h13 = (x.T @ x) / TOKENS
@@ -389,6 +404,77 @@ def run_hessian_case(args, local):
     print(json.dumps(out))
 
 
+def run_experts_case(args, local):
+    """A bounded slice of BASELINE configs[2]: --experts Kimi-class experts on one GPU, per-expert Hessians from
+    64 routed tokens (top-8 of 384 over 8192 synthetic tokens), per-tensor K in {2,3,4} drawn with probabilities
+    (0.2, 0.4, 0.4) (3.2 bpw on average), all encoded by one quantize_uniform_batches call per step."""
+    from kquant_b200 import _native
+    from kquant_b200 import exl3_encoder_backend as be
+    from kquant_b200.ldlq import make_shared_h
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _native.load()
+    E = args.experts
+    g = torch.Generator(device=device).manual_seed(77)
+    chan = torch.exp(torch.randn(HIDDEN, generator=g, device=device))
+    x_all = torch.randn((TOKENS, HIDDEN), generator=g, device=device) * chan
+    logits = torch.randn((TOKENS, 384), generator=g, device=device)
+    routed = torch.zeros((TOKENS, 384), dtype=torch.bool, device=device)
+    routed.scatter_(1, logits.topk(8, dim=1).indices, True)
+    kg = torch.Generator().manual_seed(78)
+    ks = [[(2, 3, 4)[int(torch.multinomial(torch.tensor([0.2, 0.4, 0.4]), 1, generator=kg))] for _ in range(3)]
+          for _ in range(E)]
+    experts = []
+    for e in range(E):
+        (gate, up, down), _, _ = make_triplet_weights(device, seed=5000 + e)
+        tok = torch.nonzero(routed[:, e]).flatten()[:64]
+        x = x_all[tok]
+        h13 = (x.T @ x) / x.shape[0]
+        act = torch.nn.functional.silu(x @ gate.float().T) * (x @ up.float().T)
+        h2 = (act.T @ act) / x.shape[0]
+        experts.append(([to_exl(w) for w in (gate, up, down)], h13.contiguous(), h2.contiguous()))
+    del x_all
+
+    def groups():
+        out = []
+        for e, (ws, h13, h2) in enumerate(experts):
+            qa = [quant_args(m, device, layer=e + 1) for m in ("w1", "w3", "w2")]
+            for q, K in zip(qa, ks[e]):
+                q["K"] = K
+            s13 = make_shared_h(HIDDEN, device, h13)
+            if ks[e][0] == ks[e][1]:
+                out.append(([ws[0].clone(), ws[1].clone()], [s13, s13], qa[:2]))
+            else:
+                out.append(([ws[0].clone()], [s13], qa[:1]))
+                out.append(([ws[1].clone()], [s13], qa[1:2]))
+            out.append(([ws[2].clone()], [make_shared_h(INTER, device, h2)], qa[2:]))
+        return out
+
+    weights = E * 3 * HIDDEN * INTER
+    for _ in range(args.warmup):
+        be.quantize_uniform_batches(groups())
+    torch.cuda.synchronize()
+    _native.stats.reset(timing=True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        res = be.quantize_uniform_batches(groups())
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / 1e3 / args.steps
+    vl, vbusy, vtiles, vrelax, vsum = _native.stats.viterbi_summary()
+    peak = 2.0 * _native.measure_hfma2_rate(device) / 1e12
+    proxies = [p for r in res for p, _ in r]
+    flat = [k for row in ks for k in row]
+    print(json.dumps({
+        "case": "experts", "experts": E, "weights_per_step": weights, "bpw_mean": sum(flat) / len(flat),
+        "k_counts": {k: flat.count(k) for k in (2, 3, 4)}, "ms_per_step": t * 1e3,
+        "mweights_per_s": weights / t / 1e6, "viterbi_launches_per_step": vl // max(args.steps, 1),
+        "viterbi_busy_share": vbusy / (t * args.steps),
+        "viterbi_frac_of_fp16_peak": 3.0 * vrelax / vbusy / 1e12 / peak if vbusy else None,
+        "proxy_max": max(proxies), "data": "synthetic"}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -397,14 +483,21 @@ def main():
     ap.add_argument("--impl", default="kq", choices=["kq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--case", default="triplet", choices=["triplet", "viterbi", "trace", "pack", "load", "hessian"],
+    ap.add_argument("--case", default="triplet",
+                    choices=["triplet", "experts", "viterbi", "trace", "pack", "load", "hessian"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
     ap.add_argument("--tokens", type=int, default=TOKENS, help="hessian case: samples per call")
     ap.add_argument("--dim", type=int, default=HIDDEN, help="hessian case: sample width")
+    ap.add_argument("--experts", type=int, default=8, help="experts case: experts per GPU")
     args = ap.parse_args()
+    if args.case == "triplet" and args.K != K_BITS:
+        _set_rate(args.K)
     world, rank, local = _dist()
+    if args.case == "experts":
+        run_experts_case(args, local)
+        return
     if args.case == "viterbi":
         run_viterbi_case(args, local)
         return
