@@ -28,6 +28,7 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kJobs = 2;
+constexpr int kStageBufs = 4;   // traceback row staging: buffers in the cp.async pipeline
 
 template <int K>
 struct PairMap {
@@ -291,24 +292,6 @@ struct ChainIO {
         R = c.r0 + row;
         x = tc * 16 + col;
     }
-    __device__ __forceinline__ float load(int64_t tile, int j) const {
-        const int i = find(tile);
-        const kq_chain_item& c = it[i];
-        int64_t R, x, tc;
-        locate(c, tile - start[i], j, R, x, tc);
-        const int64_t n = c.size_n, k = c.size_k;
-        float s = 0.f;
-        const float* lp = c.L + (c.r0 + 16) * k + R;
-        const float* ep = c.err + (c.r0 + 16) * n + x;
-#pragma unroll 8
-        for (int64_t q = c.r0 + 16; q < c.end; ++q) {
-            s = fmaf(__ldg(lp), __ldcg(ep), s);
-            lp += k;
-            ep += n;
-        }
-        const float comp = c.P[R * n + x] + s;
-        return c.W[R * n + x] + comp;
-    }
     // Element j of tile (2q + t) for every thread of the CTA (t = tid / 256,
     // j = tid % 256), both tiles of the pair at once: the feedback rows of
     // each tile (L[r0+16+i][r0..r0+15], err[r0+16+i][16 tile columns]) go to
@@ -550,28 +533,46 @@ pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
             if (phase[1] == PH_TP) { rem1 = C - step[1]; row1 = C - 1 - step[1]; }
             if (phase[1] == PH_TF) { rem1 = 256 - step[1]; row1 = 255 - step[1]; }
             const int ntb = (rem0 > 0) + (rem1 > 0);
-            const int cap = (2 * M::NODES * 4) / (ntb * M::ROW_BYTES);    // rows per job per chunk
+            // Rows stream through kStageBufs buffers with cp.async, kStageBufs - 1
+            // chunks in flight while the lanes walk the oldest: the copy runs at
+            // memory bandwidth instead of one latency-bound chunk at a time.
+            const int cap = (2 * M::NODES * 4) / (ntb * M::ROW_BYTES * kStageBufs);   // rows per job per buffer
+            const int nchunks = (max(rem0, rem1) + cap - 1) / cap;
             uint8_t* stage = reinterpret_cast<uint8_t*>(cost);
-            uint8_t* slot0 = stage;
-            uint8_t* slot1 = stage + (rem0 > 0 ? (size_t)cap * M::ROW_BYTES : 0);
-            while (rem0 > 0 || rem1 > 0) {
-                const int R0 = min(rem0, cap), R1 = min(rem1, cap);
-                // rows [row - R + 1, row] are contiguous in the job's decision area
-                if (R0 > 0) {
-                    const uint4* src = reinterpret_cast<const uint4*>(dec_job(0) + (size_t)(row0 - R0 + 1) * M::ROW_BYTES);
-                    uint4* dst = reinterpret_cast<uint4*>(slot0);
-                    for (int i = tid; i < R0 * M::ROW_BYTES / 16; i += kThreads) dst[i] = __ldcg(src + i);
+            const size_t buf_bytes = (size_t)ntb * cap * M::ROW_BYTES;
+            const int slot_of1 = (rem0 > 0) ? 1 : 0;                     // job 1's slot in a buffer
+            auto issue = [&](int c) {
+                if (c < nchunks) {
+                    uint8_t* buf = stage + (size_t)(c % kStageBufs) * buf_bytes;
+#pragma unroll
+                    for (int j = 0; j < kJobs; ++j) {
+                        const int rem = j ? rem1 : rem0, top = j ? row1 : row0;
+                        const int lo = c * cap, R = min(cap, rem - lo);
+                        if (R <= 0) continue;
+                        const uint8_t* src = dec_job(j) + (size_t)(top - lo - R + 1) * M::ROW_BYTES;
+                        uint8_t* dst = buf + (size_t)(j ? slot_of1 : 0) * cap * M::ROW_BYTES;
+                        const int units = R * M::ROW_BYTES / 16;
+                        for (int i = tid; i < units; i += kThreads) {
+                            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                         ::"r"((uint32_t)__cvta_generic_to_shared(dst + 16 * i)), "l"(src + 16 * i)
+                                         : "memory");
+                        }
+                    }
                 }
-                if (R1 > 0) {
-                    const uint4* src = reinterpret_cast<const uint4*>(dec_job(1) + (size_t)(row1 - R1 + 1) * M::ROW_BYTES);
-                    uint4* dst = reinterpret_cast<uint4*>(slot1);
-                    for (int i = tid; i < R1 * M::ROW_BYTES / 16; i += kThreads) dst[i] = __ldcg(src + i);
-                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+            };
+#pragma unroll
+            for (int c = 0; c < kStageBufs - 1; ++c) issue(c);
+            for (int c = 0; c < nchunks; ++c) {
+                issue(c + kStageBufs - 1);
+                asm volatile("cp.async.wait_group %0;" ::"n"(kStageBufs - 1) : "memory");
                 __syncthreads();
                 if (my_tb) {
-                    const int R = tb_job ? R1 : R0;
-                    const int first = (tb_job ? row1 : row0) - R + 1;
-                    const uint8_t* sl = tb_job ? slot1 : slot0;
+                    const int rem = tb_job ? rem1 : rem0, top = tb_job ? row1 : row0;
+                    const int lo = c * cap, R = min(cap, rem - lo);
+                    const int first = top - lo - R + 1;
+                    const uint8_t* sl = stage + (size_t)(c % kStageBufs) * buf_bytes +
+                                        (size_t)(tb_job ? slot_of1 : 0) * cap * M::ROW_BYTES;
                     for (int s2 = 0; s2 < R; ++s2) {
                         int owner, word, sh;
                         M::locate(tb.node, tb_tile, owner, word, sh);
@@ -584,11 +585,8 @@ pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
                     }
                 }
                 __syncthreads();
-                rem0 -= R0;
-                row0 -= R0;
-                rem1 -= R1;
-                row1 -= R1;
             }
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
             if (my_tb && my_phase == PH_TP) {
                 es_sh[tb_job * 2 + tb_tile] = tb.node;
                 tb.row = 255;
