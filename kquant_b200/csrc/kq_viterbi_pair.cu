@@ -41,6 +41,7 @@ struct PairMap {
     static constexpr int NPT = 2 * PB * G;                  // nodes per thread (8, 16, 32)
     static constexpr int DB = (K == 2) ? 2 : 4;             // decision bits per (node, tile)
     static constexpr int TILE_WORDS = NPT * DB / 32;        // 32-bit words per tile per thread
+    static constexpr int GPW = 32 / (2 * PB * DB);          // block parts per decision word
     static constexpr int WORD_BYTES = 2 * TILE_WORDS * 4;   // both tiles
     static constexpr int ROW_BYTES = kThreads * WORD_BYTES;
 
@@ -62,10 +63,14 @@ struct PairMap {
             g = h >> 9;
             j = e & (2 * PB - 1);
         }
-        const int bit = (g * 2 * PB + j) * DB;
-        word = t * TILE_WORDS + (bit >> 5);
-        shift = bit & 31;
+        // Word layout: block parts g are packed GPW to a word; within a part,
+        // even nodes (half2 lane 0) sit in the low 16 bits and odd nodes (lane 1)
+        // in the high 16 bits, DB bits per node.
+        word = t * TILE_WORDS + g / GPW;
+        shift = (j & 1) * 16 + (g % GPW) * PB * DB + (j >> 1) * DB;
     }
+    // Bit offset (within its 16-bit lane) of node pair p of block part g.
+    __host__ __device__ static constexpr int field(int g, int p) { return (g % GPW) * PB * DB + p * DB; }
 };
 
 template <int K, bool DEC, int STEP0>
@@ -117,7 +122,8 @@ __device__ __forceinline__ void pair_step(
                     if constexpr (DEC) { idA[p] = 0u; idB[p] = 0u; }
                 } else {
                     if constexpr (DEC) {
-                        const uint32_t kk = (uint32_t)(k * 0x10001);
+                        // k placed at its node's final bit position in the decision word
+                        const uint32_t kk = ((uint32_t)k << M::field(g, p)) * 0x10001u;
                         const uint32_t ltA = __hlt2_mask(eA, mnA[p]);
                         const uint32_t ltB = __hlt2_mask(eB, mnB[p]);
                         idA[p] = (ltA & kk) | (~ltA & idA[p]);
@@ -150,13 +156,11 @@ __device__ __forceinline__ void pair_step(
             dst[0] = make_uint4(v[0], v[1], v[2], v[3]);
         }
         if constexpr (DEC) {
+            // decisions are already at their bit positions: OR the pairs in
 #pragma unroll
             for (int p = 0; p < PB; ++p) {
-                const int bit = (g * 2 * PB + 2 * p) * M::DB;
-                const uint32_t a = (idA[p] & 0xFFFFu) | ((idA[p] >> 16) << M::DB);
-                const uint32_t b = (idB[p] & 0xFFFFu) | ((idB[p] >> 16) << M::DB);
-                words[bit >> 5] |= a << (bit & 31);
-                words[M::TILE_WORDS + (bit >> 5)] |= b << (bit & 31);
+                words[g / M::GPW] |= idA[p];
+                words[M::TILE_WORDS + g / M::GPW] |= idB[p];
             }
         }
     }
