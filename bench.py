@@ -475,6 +475,27 @@ def run_experts_case(args, local):
         "proxy_max": max(proxies), "data": "synthetic"}))
 
 
+def run_profile_case(args, local):
+    """Kernel list of one warm triplet step (torch.profiler / CUPTI device times): every launch of the step with
+    its device time, grouped by kernel, as a launch list without a replaying profiler."""
+    from torch.profiler import ProfilerActivity, profile
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    hf, h13, h2 = make_triplet(device, seed=1234)
+    exl = [to_exl(w) for w in hf]
+    for _ in range(max(args.warmup, 1)):
+        encode_triplet([w.clone() for w in exl], h13, h2, device)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        encode_triplet([w.clone() for w in exl], h13, h2, device)
+        torch.cuda.synchronize()
+    rows = sorted(prof.key_averages(), key=lambda e: -e.device_time_total)
+    total = sum(e.device_time_total for e in rows)
+    print(json.dumps({"case": "profile", "device_ms": total / 1e3, "kernels": [
+        {"name": e.key[:120], "launches": e.count, "ms": e.device_time_total / 1e3,
+         "share": e.device_time_total / total} for e in rows[:args.top]]}, indent=1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -484,19 +505,23 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--case", default="triplet",
-                    choices=["triplet", "experts", "viterbi", "trace", "pack", "load", "hessian"],
+                    choices=["triplet", "experts", "viterbi", "trace", "pack", "load", "hessian", "profile"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
     ap.add_argument("--tokens", type=int, default=TOKENS, help="hessian case: samples per call")
     ap.add_argument("--dim", type=int, default=HIDDEN, help="hessian case: sample width")
     ap.add_argument("--experts", type=int, default=8, help="experts case: experts per GPU")
+    ap.add_argument("--top", type=int, default=25, help="profile case: kernels listed")
     args = ap.parse_args()
     if args.case == "triplet" and args.K != K_BITS:
         _set_rate(args.K)
     world, rank, local = _dist()
     if args.case == "experts":
         run_experts_case(args, local)
+        return
+    if args.case == "profile":
+        run_profile_case(args, local)
         return
     if args.case == "viterbi":
         run_viterbi_case(args, local)
