@@ -1484,12 +1484,14 @@ def quantize_qsrt_batch(weights: list[torch.Tensor], H_datas: list[dict], quant_
 
 
 def _uniform_prepare(weights: list[torch.Tensor], H_datas: list[dict], quant_args_list: list[dict],
-                     verbose: bool):
+                     verbose: bool, search: bool = True):
     """Phase 1 of quantize_uniform_batch: H finalisation, regularisation, global scale.
 
     Consumes the RNG exactly as the reference does (reseeded per matrix).
     Returns the batch state; ``state["ldlq"]`` is None when every member fell
-    back (``state["results"]`` is then complete).
+    back (``state["results"]`` is then complete).  With ``search=False`` it
+    stops before the scale search, leaving ``state["samples"]`` for a search
+    shared with other batches (:func:`_uniform_apply_scales` then finishes).
     """
     if any("mixed_rate_axis" in a or "mixed_tile_bits" in a for a in quant_args_list):
         raise ValueError("mixed-rate LDLQ is currently supported by quantize_qsrt, not the same-K batch API")
@@ -1533,7 +1535,25 @@ def _uniform_prepare(weights: list[torch.Tensor], H_datas: list[dict], quant_arg
         apply_out, wr, _, su, sv = regularize(w, su, sv, qa, verbose, H_diag, None, skip_g_scale=True)
         regs[t] = [wr, su, sv, apply_out]
         weights[t] = None
-    scales = g_scale_search_batch([sample_scale_tiles(regs[t][0]) for t in batch], qa0)
+    state.update(regs=regs, samples=[sample_scale_tiles(regs[t][0]) for t in batch])
+    if not search:
+        return state
+    return _uniform_apply_scales(state, g_scale_search_batch(state["samples"], qa0))
+
+
+def _search_key(quant_args: dict):
+    """Launch-compatibility key of a scale search: same K, codebook, context and devices."""
+    bits = int(quant_args["K"])
+    kind, lut = _tile_codebook(quant_args, bits)
+    return (bits, kind, id(lut), int(quant_args.get("tailbite_context", 128)), tuple(quant_args["devices"]))
+
+
+def _uniform_apply_scales(state: dict, scales):
+    """Phase 1b: apply the searched global scales and set up the LDLQ operands."""
+    batch, regs, finalized = state["batch"], state["regs"], state["finalized"]
+    quant_args_list, device, shared_H = state["quant_args_list"], state["device"], state["shared_H"]
+    qa0 = quant_args_list[0]
+    state.pop("samples", None)
     g_scales = {}
     for t, (g, _) in zip(batch, scales):
         regs[t][0] *= g
@@ -1666,9 +1686,10 @@ def quantize_uniform_batches(groups, verbose: bool = False):
 
     ``groups`` is a list of (weights, H_datas, quant_args_list).  The
     preparation phases run in order (same RNG seeding as sequential calls),
-    then every matrix of every group is one set of chains in a single
-    chain-engine run (:func:`_chain_traverse`), then the outputs are built in
-    order.  Results equal the sequential calls bit for bit: a chain step's
+    the global-scale searches of all groups with the same (K, codebook,
+    context) share their tile launches, then every matrix of every group is
+    one set of chains in a single chain-engine run (:func:`_chain_traverse`),
+    then the outputs are built in order.  Results equal the sequential calls bit for bit: a chain step's
     arithmetic does not depend on which other chains share its launch.
     Returns one result list per group.  Groups spanning several devices run
     sequentially.
@@ -1676,7 +1697,20 @@ def quantize_uniform_batches(groups, verbose: bool = False):
     groups = [(list(w), list(h), list(q)) for w, h, q in groups]
     if any(len(q[0]["devices"]) > 1 for _, _, q in groups) or len(groups) < 2:
         return [quantize_uniform_batch(w, h, q, None, verbose) for w, h, q in groups]
-    states = [_uniform_prepare(w, h, q, verbose) for w, h, q in groups]
+    states = [_uniform_prepare(w, h, q, verbose, search=False) for w, h, q in groups]
+    # one scale search per (K, codebook, context, devices) over every group's samples
+    pending = [i for i, st in enumerate(states) if st.get("samples")]
+    by_key: dict = {}
+    for i in pending:
+        by_key.setdefault(_search_key(states[i]["quant_args_list"][0]), []).append(i)
+    for idx in by_key.values():
+        samples = [t for i in idx for t in states[i]["samples"]]
+        scales = g_scale_search_batch(samples, states[idx[0]]["quant_args_list"][0])
+        at = 0
+        for i in idx:
+            n = len(states[i]["samples"])
+            _uniform_apply_scales(states[i], scales[at:at + n])
+            at += n
     live = [i for i, st in enumerate(states) if st["ldlq"] is not None]
     out = {}
     by_device: dict = {}
