@@ -1,0 +1,91 @@
+"""CPU tests of the LDLQ chain engine's scheduler (kquant_b200.exl3_encoder_backend._chain_traverse).
+
+The launch function is replaced by a recorder and the matrices are meta tensors,
+so only the host logic runs: every chain walks its 16-row steps in the backward
+buffer order of kquant/exl3_encoder_backend.py:389-505 exactly once, every launch
+holds at most 2 x SMs tiles and KQ_CHAIN_MAX_ITEMS items of one (K, codebook,
+context) key, and the buffer-end feedback updates happen after a buffer's last
+step, on the chain's own columns.
+"""
+import torch
+
+from kquant_b200 import _native
+from kquant_b200 import exl3_encoder_backend as be
+
+
+class _Member:
+    def __init__(self, k, n, key, buffer_rows=128):
+        self.k, self.n = k, n
+        self.W = torch.empty((k, n), device="meta")
+        self.P = torch.empty((k, n), device="meta")
+        self.E = torch.empty((k, n), device="meta")
+        self.wq = torch.empty((k, n), device="meta")
+        self.L = torch.empty((k, k), device="meta")
+        self.enc = torch.empty((k // 16, n // 16, 256), dtype=torch.int16, device="meta")
+        self.buffer_rows = buffer_rows
+        self.tf32 = False
+        self.key = key
+        self.labels = torch.empty(65536, dtype=torch.int16, device="meta")
+
+
+def _run(monkeypatch, members, sms=148):
+    launches = []
+
+    def fake_step(items, K, labels, ctx, device, max_ctas=0):
+        launches.append([(it.size_k, it.size_n, it.r0, it.end, it.tile_col0, it.n_tiles, K, ctx) for it in items])
+
+    class _Props:
+        multi_processor_count = sms
+
+    monkeypatch.setattr(_native, "ldlq_chain_step", fake_step)
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda device: _Props())
+    trims = []
+    real_advance = be._Chain.advance
+
+    def advance(self):
+        r0, end = self.steps[self.pos]
+        if r0 == end - self.m.buffer_rows and r0 > 0:
+            trims.append((id(self.m), self.tile_col0, r0, end))
+        real_advance(self)
+
+    monkeypatch.setattr(be._Chain, "advance", advance)
+    be._chain_traverse(members, torch.device("cpu"))
+    return launches, trims
+
+
+def test_triplet_schedule_is_valid_and_packed(monkeypatch):
+    key = (3, 1, 128)
+    gate_up = _Member(7168, 4096, key)
+    down = _Member(2048, 7168, key)
+    launches, trims = _run(monkeypatch, [gate_up, down])
+    cap = 2 * 148
+    seen = {}
+    for items in launches:
+        assert 1 <= len(items) <= _native.KQ_CHAIN_MAX_ITEMS
+        assert sum(i[5] for i in items) <= cap
+        assert len({(i[6], i[7]) for i in items}) == 1
+        cols = [(i[0], i[1], i[4]) for i in items]
+        assert len(cols) == len(set(cols))                      # one step per chain per launch
+        for k, n, r0, end, c0, nt, _, _ in items:
+            seen.setdefault((k, n, c0), []).append((r0, end))
+    # every chain: all k/16 steps, backward over 128-row buffers, each exactly once
+    for (k, n, c0), steps in seen.items():
+        expect = [(end - 128 + le - 16, end) for end in range(k, 0, -128) for le in range(128, 0, -16)]
+        assert steps == expect
+    assert len(seen) == 4096 // 16 // 32 + 7168 // 16 // 32
+    # 172,032 tiles: the lower bound is 582 single-wave launches; the schedule stays within 3 %
+    assert sum(sum(i[5] for i in items) for items in launches) == 7168 // 16 * 4096 // 16 + 2048 // 16 * 7168 // 16
+    assert len(launches) <= 600
+    # trims: one per chain per buffer except the first rows
+    assert len(trims) == (4096 // 512) * (7168 // 128 - 1) + (7168 // 512) * (2048 // 128 - 1)
+
+
+def test_keys_never_share_a_launch_and_narrow_tail_chains(monkeypatch):
+    a = _Member(256, 16 * 40, (2, 1, 128))          # 40 tile columns: chains of 32 + 8
+    b = _Member(512, 16 * 32, (4, 1, 64))
+    launches, _ = _run(monkeypatch, [a, b], sms=16)
+    widths = {i[5] for items in launches for i in items if i[1] == 16 * 40}
+    assert widths == {32, 8}
+    for items in launches:
+        assert len({(i[6], i[7]) for i in items}) == 1
+        assert sum(i[5] for i in items) <= 2 * 16 or len(items) == 1
