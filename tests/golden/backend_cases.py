@@ -23,15 +23,18 @@ def make_inputs(case, device):
     return w.to(device), h.to(device), args
 
 
-# quantize_uniform_batch fixture: two matrices sharing one H (gate/up style)
+# quantize_uniform_batch fixtures: two matrices sharing one H (gate/up style), and
+# two matrices with distinct Hessians (stacked members)
 UNIFORM_CASES = {
     "uniform_pair_k3": {"k": 256, "n": 256, "K": 3, "ctx": 128, "seed": 13},
+    "uniform_distinct_k4": {"k": 256, "n": 128, "K": 4, "ctx": 32, "seed": 14, "distinct": True},
 }
 
 
 def make_uniform_inputs(case, device):
-    w1, h, a1 = make_inputs(case, device)
-    w2, _, _ = make_inputs(dict(case, seed=case["seed"] + 100), device)
+    """([w1, w2], [h1, h2], [args1, args2]); h2 is h1 unless the case has distinct Hessians."""
+    w1, h1, a1 = make_inputs(case, device)
+    w2, h2, _ = make_inputs(dict(case, seed=case["seed"] + 100), device)
     a2 = dict(a1, sv_seed=a1["sv_seed"] + 1)
     a2["sqg_e4m3_luts_by_bits"] = a1["sqg_e4m3_luts_by_bits"]
-    return [w1, w2], h, [a1, a2]
+    return [w1, w2], [h1, h2 if case.get("distinct") else h1], [a1, a2]

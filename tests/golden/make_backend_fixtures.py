@@ -9,7 +9,7 @@ no-ops, and the tile quantizer is the C oracle (a restatement of the reference
 Viterbi kernel, pinned against it bit for bit on the GPU).  Random sign draws
 use the CPU generator; the GPU test reproduces them the same way.
 
-Usage: python tests/golden/make_backend_fixtures.py /path/to/reference
+Usage: python tests/golden/make_backend_fixtures.py /path/to/reference [case ...]
 Writes tests/golden/backend_<case>.npz (quantize_qsrt cases and the
 quantize_uniform_batch cases).
 """
@@ -86,7 +86,10 @@ def _load_reference_backend(ref_root: Path):
 def main():
     ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
     be = _load_reference_backend(ref_root)
+    only = set(sys.argv[2:])
     for name, case in CASES.items():
+        if only and name not in only:
+            continue
         w, h, args = make_inputs(case, "cpu")
         from kquant.ldlq import make_shared_h
         H_data = make_shared_h(w.shape[0], torch.device("cpu"), h)
@@ -100,11 +103,14 @@ def main():
             states=unpack_trellis_states(out["trellis"], args["K"]).numpy())
         print(name, "proxy", proxy, "g_scale", args["g_scale"])
     for name, case in UNIFORM_CASES.items():
-        ws, h, args = make_uniform_inputs(case, "cpu")
+        if only and name not in only:
+            continue
+        ws, hs, args = make_uniform_inputs(case, "cpu")
         from kquant.ldlq import make_shared_h
         from kquant.qsrt import unpack_trellis_states
-        shared = make_shared_h(ws[0].shape[0], torch.device("cpu"), h)
-        res = be.quantize_uniform_batch([w.clone() for w in ws], [shared, shared], args)
+        shared = make_shared_h(ws[0].shape[0], torch.device("cpu"), hs[0])
+        H_datas = [shared, shared] if hs[1] is hs[0] else [shared, make_shared_h(ws[1].shape[0], torch.device("cpu"), hs[1])]
+        res = be.quantize_uniform_batch([w.clone() for w in ws], H_datas, args)
         fields = {}
         for t, (proxy, out) in enumerate(res):
             fields.update({f"proxy{t}": np.array(proxy), f"suh{t}": out["suh"].numpy(), f"svh{t}": out["svh"].numpy(),

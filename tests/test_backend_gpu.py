@@ -187,3 +187,11 @@ def test_chain_engine_long_buffers_and_stacked_members(cuda_device):
             st = _native.unpack_trellis_states(out["trellis"], K).view(-1, 256).long() & 0xFFFF
             prev = torch.roll(st, 1, dims=1)
             assert torch.equal(((prev << K) | (st & ((1 << K) - 1))) & 0xFFFF, st)
+
+
+def test_chain_step_against_oracle(cuda_device):
+    """One kq_ldlq_chain_step launch (in-kernel feedback) against the oracle, bit for bit (smoke's check)."""
+    import numpy as np
+
+    import __graft_entry__
+    __graft_entry__._smoke_chain_step(cuda_device, np.random.default_rng(5))

@@ -66,9 +66,10 @@ def test_backend_matches_reference_fixture(cuda_device, cpu_sign_draws, name):
 def test_uniform_batch_matches_reference_fixture(cuda_device, cpu_sign_draws, name):
     """quantize_uniform_batch (the LDLQ chain engine) against the reference's quantize_uniform_batch."""
     ref = np.load(GOLDEN / f"backend_{name}.npz")
-    ws, h, args = make_uniform_inputs(UNIFORM_CASES[name], cuda_device)
-    shared = make_shared_h(ws[0].shape[0], cuda_device, h)
-    res = be.quantize_uniform_batch([w.clone() for w in ws], [shared, shared], args)
+    ws, hs, args = make_uniform_inputs(UNIFORM_CASES[name], cuda_device)
+    shared = make_shared_h(ws[0].shape[0], cuda_device, hs[0])
+    H_datas = [shared, shared] if hs[1] is hs[0] else [shared, make_shared_h(ws[1].shape[0], cuda_device, hs[1])]
+    res = be.quantize_uniform_batch([w.clone() for w in ws], H_datas, args)
     torch.cuda.synchronize()
     for t, (proxy, out) in enumerate(res):
         ref_proxy = float(ref[f"proxy{t}"])
@@ -82,7 +83,11 @@ def test_uniform_batch_matches_reference_fixture(cuda_device, cpu_sign_draws, na
         }
         print(name, t, json.dumps(stats))
         assert stats["proxy_rel"] < 0.01
-        assert stats["g_scale_rel"] < 1e-3
-        assert stats["suh_equal"] > 0.99 and stats["svh_equal"] > 0.99
+        assert stats["g_scale_rel"] < 1e-4
+        # The global scale comes from a parabola through fp32 MSE sums, summed in a
+        # different order on the CPU (fixture) than on the GPU; on a flat MSE curve
+        # (uniform_distinct_k4 member 0: 2e-5 relative) that flips the fp16 rounding
+        # of a few percent of the suh = su / g entries, and the codes downstream of them.
+        assert stats["suh_equal"] > 0.9 and stats["svh_equal"] > 0.9
         if stats["suh_equal"] == 1.0 and stats["svh_equal"] == 1.0:
             assert stats["states_equal"] == 1.0
