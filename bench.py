@@ -475,6 +475,43 @@ def run_experts_case(args, local):
         "proxy_max": max(proxies), "data": "synthetic"}))
 
 
+def run_chain_case(args, local):
+    """The LDLQ chain engine alone on the triplet's shapes (gate+up [7168 x 4096] and down [2048 x 7168], K=--K):
+    synthetic W, unit-lower-triangular L and zero feedback state, every step of every chain.  Reports launches,
+    mean launch time (CUDA events) and tiles/s; the profiling case for pair_kernel<K, ChainIO>."""
+    from kquant_b200 import _native
+    from kquant_b200 import exl3_encoder_backend as be
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _native.load()
+    g = torch.Generator(device=device).manual_seed(9)
+
+    def member(k, n):
+        W = torch.randn((k, n), generator=g, device=device) * 0.5
+        L = torch.tril(torch.randn((k, k), generator=g, device=device) * 0.01, -1) + torch.eye(k, device=device)
+        qa = quant_args("w1", device)
+        qa["K"] = args.K
+        return be._ChainMember(W, L, torch.empty_like(W),
+                               torch.empty((k // 16, n // 16, 256), dtype=torch.int16, device=device), qa)
+
+    shapes = [(HIDDEN, 2 * INTER), (INTER, HIDDEN)]
+    for _ in range(max(args.warmup, 1)):
+        be._chain_traverse([member(k, n) for k, n in shapes], device)
+    members = [member(k, n) for k, n in shapes]
+    torch.cuda.synchronize()
+    _native.stats.reset(timing=True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    be._chain_traverse(members, device)
+    b.record()
+    torch.cuda.synchronize()
+    vl, vbusy, vtiles, vrelax, vsum = _native.stats.viterbi_summary()
+    peak = 2.0 * _native.measure_hfma2_rate(device) / 1e12
+    print(json.dumps({"case": "chain", "K": args.K, "launches": vl, "tiles": vtiles,
+                      "ms_total": a.elapsed_time(b), "ms_per_launch": vsum / vl * 1e3,
+                      "tiles_per_s": vtiles / vbusy, "frac_of_fp16_alu_peak": 3.0 * vrelax / vbusy / 1e12 / peak}))
+
+
 def run_profile_case(args, local):
     """Kernel list of one warm triplet step (torch.profiler / CUPTI device times): every launch of the step with
     its device time, grouped by kernel, as a launch list without a replaying profiler."""
@@ -505,7 +542,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--case", default="triplet",
-                    choices=["triplet", "experts", "viterbi", "trace", "pack", "load", "hessian", "profile"],
+                    choices=["triplet", "experts", "chain", "viterbi", "trace", "pack", "load", "hessian", "profile"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
@@ -522,6 +559,9 @@ def main():
         return
     if args.case == "profile":
         run_profile_case(args, local)
+        return
+    if args.case == "chain":
+        run_chain_case(args, local)
         return
     if args.case == "viterbi":
         run_viterbi_case(args, local)
@@ -575,6 +615,8 @@ def main():
     elapsed = _allreduce_max(start.elapsed_time(end) / 1e3, world)
     launches = _native.stats.launches
     vl, vsec, vtiles, vrelax, vsum = _native.stats.viterbi_summary()
+    sizes = sorted(n for _, _, n, _ in _native.stats.events)
+    median_tiles = sizes[len(sizes) // 2] if sizes else 0
     _native.stats.reset(timing=False)
     clocks = clk.summary()
 
@@ -615,7 +657,8 @@ def main():
     tpath = ROOT / "profiles" / "viterbi_dram_bytes_per_tile.txt"
     if tpath.exists() and vl:
         try:
-            traffic = float(tpath.read_text().split()[0]) * vtiles / vl
+            # per launch of the dominant kernel (the LDLQ chain launches, the median launch size)
+            traffic = float(tpath.read_text().split()[0]) * median_tiles
         except (ValueError, IndexError):
             traffic = None
     line = {
