@@ -88,6 +88,10 @@ def test_uniform_batch_matches_reference_fixture(cuda_device, cpu_sign_draws, na
         # different order on the CPU (fixture) than on the GPU; on a flat MSE curve
         # (uniform_distinct_k4 member 0: 2e-5 relative) that flips the fp16 rounding
         # of a few percent of the suh = su / g entries, and the codes downstream of them.
+        # A global scale a few ulp off (uniform_distinct_k4 member 1: 4e-7) changes
+        # W * g in the last bits, and the LDLQ feedback carries the resulting code
+        # differences up the matrix; codes are bit-exact when all scales agree exactly.
         assert stats["suh_equal"] > 0.9 and stats["svh_equal"] > 0.9
-        if stats["suh_equal"] == 1.0 and stats["svh_equal"] == 1.0:
+        assert stats["states_equal"] > 0.8
+        if stats["suh_equal"] == 1.0 and stats["svh_equal"] == 1.0 and stats["g_scale_rel"] == 0.0:
             assert stats["states_equal"] == 1.0
