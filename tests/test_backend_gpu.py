@@ -195,3 +195,27 @@ def test_chain_step_against_oracle(cuda_device):
 
     import __graft_entry__
     __graft_entry__._smoke_chain_step(cuda_device, np.random.default_rng(5))
+
+
+@pytest.mark.parametrize("B,k,n", [(1, 1024, 512), (2, 512, 384)])
+def test_chain_engine_equals_cublas_feedback_path(cuda_device, B, k, n):
+    """Chain engine (feedback product summed in the kernel) == the fused-step path whose feedback is the
+    reference's cuBLAS baddbmm (kquant/exl3_encoder_backend.py:389-505), codes and What bit for bit."""
+    dev = cuda_device
+    W = torch.stack([_problem(dev, k=k, n=n, seed=40 + b)[0] for b in range(B)]) * 25
+    Ls = []
+    for b in range(B):
+        _, h = _problem(dev, k=k, n=n, seed=50 + b)
+        L, _ = be.block_ldl(h.clone(), 16, {"devices": [str(dev)], "sigma_reg": 0.025}, False)
+        Ls.append(L)
+    Ls = torch.stack(Ls).contiguous()
+    qa = _args(dev)
+    wq_c = torch.empty_like(W)
+    enc_c = torch.empty((B, k // 16, n // 16, 256), dtype=torch.int16, device=dev)
+    members = [be._ChainMember(W[b], Ls[b], wq_c[b], enc_c[b], qa) for b in range(B)]
+    be._chain_traverse(members, dev)
+    plan = be._RatePlan(3, None, B, n // 16, dev)
+    wq_s, enc_s, _ = be._ldlq_traverse(W, Ls, qa, plan, buffer_rows=128, tf32=False)
+    torch.cuda.synchronize()
+    assert torch.equal(enc_c, enc_s)
+    assert torch.equal(wq_c, wq_s)
