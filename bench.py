@@ -475,6 +475,74 @@ def run_experts_case(args, local):
         "proxy_max": max(proxies), "data": "synthetic"}))
 
 
+def run_qsrt_case(args, local):
+    """kquant's production call (kquant/pack/qsrt_encoder.py:824-832): quantize_qsrt_batch over --experts experts
+    x the three rate-transfer modes R0/R1/R2, once for gate ([7168 x 2048], n-axis records) and once for down
+    ([2048 x 7168], k-axis records), per-expert Hessians from 64 routed tokens.  Reports source weights/s (each
+    source encoded at all three candidate rates) and candidate weights/s."""
+    from kquant_b200 import _native
+    from kquant_b200 import exl3_encoder_backend as be
+    from kquant_b200 import qsrt
+    from kquant_b200.ldlq import make_shared_h
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _native.load()
+    E = args.experts
+    g = torch.Generator(device=device).manual_seed(79)
+    chan = torch.exp(torch.randn(HIDDEN, generator=g, device=device))
+    srcs = {"w1": [], "w2": []}
+    hs = {"w1": [], "w2": []}
+    for e in range(E):
+        (gate, up, down), _, _ = make_triplet_weights(device, seed=6000 + e)
+        x = torch.randn((64, HIDDEN), generator=g, device=device) * chan
+        act = torch.nn.functional.silu(x @ gate.float().T) * (x @ up.float().T)
+        srcs["w1"].append(to_exl(gate))
+        srcs["w2"].append(to_exl(down))
+        hs["w1"].append(((x.T @ x) / 64).contiguous())
+        hs["w2"].append(((act.T @ act) / 64).contiguous())
+
+    def groups(matrix):
+        axis = qsrt.matrix_rate_axis(matrix)
+        out = []
+        for e in range(E):
+            base = quant_args(matrix, device, layer=e + 1)
+            cands = []
+            for mode in qsrt.RATE_TRANSFER_MODES:
+                # the modes' record maps cover 24 records of 128 channels; this expert's intermediate
+                # size holds INTER / 128 of them (records come in K2/K4 pairs, so the cut keeps 3 bpw)
+                rec = qsrt.record_bits(mode)[:INTER // 128]
+                bits = tuple(b for b in rec for _ in range(8))
+                cands.append(dict(base, mixed_rate_axis=axis, mixed_tile_bits=bits))
+            out.append(cands)
+        return out
+
+    def step():
+        for matrix, k in (("w1", HIDDEN), ("w2", INTER)):
+            be.quantize_qsrt_batch([w.clone() for w in srcs[matrix]],
+                                   [make_shared_h(k, device, h) for h in hs[matrix]], groups(matrix))
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    _native.stats.reset(timing=True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / 1e3 / args.steps
+    vl, vbusy, vtiles, vrelax, vsum = _native.stats.viterbi_summary()
+    peak = 2.0 * _native.measure_hfma2_rate(device) / 1e12
+    weights = E * 2 * HIDDEN * INTER
+    print(json.dumps({"case": "qsrt", "experts": E, "matrices": "gate (n-axis) + down (k-axis)", "modes": "R0,R1,R2",
+                      "ms_per_step": t * 1e3, "source_mweights_per_s": weights / t / 1e6,
+                      "candidate_mweights_per_s": 3 * weights / t / 1e6,
+                      "viterbi_launches_per_step": vl // max(args.steps, 1),
+                      "viterbi_busy_share": vbusy / (t * args.steps),
+                      "viterbi_frac_of_fp16_peak": 3.0 * vrelax / vbusy / 1e12 / peak if vbusy else None}))
+
+
 def run_chain_case(args, local):
     """The LDLQ chain engine alone on the triplet's shapes (gate+up [7168 x 4096] and down [2048 x 7168], K=--K):
     synthetic W, unit-lower-triangular L and zero feedback state, every step of every chain.  Reports launches,
@@ -542,7 +610,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--case", default="triplet",
-                    choices=["triplet", "experts", "chain", "viterbi", "trace", "pack", "load", "hessian", "profile"],
+                    choices=["triplet", "experts", "qsrt", "chain", "viterbi", "trace", "pack", "load", "hessian",
+                             "profile"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=1184)
     ap.add_argument("--K", type=int, default=K_BITS)
@@ -562,6 +631,9 @@ def main():
         return
     if args.case == "chain":
         run_chain_case(args, local)
+        return
+    if args.case == "qsrt":
+        run_qsrt_case(args, local)
         return
     if args.case == "viterbi":
         run_viterbi_case(args, local)

@@ -130,6 +130,9 @@ typedef struct {
     int64_t size_k, size_n;
     int64_t r0, end;
     int64_t tile_col0, n_tiles;
+    const uint16_t* labels;   /* binary16 label table of this item's codebook at rate K (kq_build_labels) */
+    int32_t K;                /* 2, 3 or 4 */
+    int32_t reserved;         /* 0 */
 } kq_chain_item;
 
 #define KQ_CHAIN_MAX_ITEMS 32
@@ -146,11 +149,15 @@ typedef struct {
  * share the launch.  Replaces the per-step feedback + quantize of
  * kquant/exl3_encoder_backend.py:389-505 (ldlq) / :1495-1583 (ldlq_batched);
  * the buffer-end update P[:begin] += L^T err stays with the caller.
- * All items use the same K, labels and context; workspace as
- * kq_viterbi_encode for the total tile count; max_ctas as kq_ldlq_step_encode.
+ * Items carry their own K and label table.  When they all share K the
+ * launch may hold any number of tiles; items of different K share one
+ * launch only if it is a single wave (at most 2 tiles per SM) and every item
+ * starts at an even tile, so that each CTA's tile pair has one K.  Workspace
+ * as kq_viterbi_encode (K = 3) for the total tile count; max_ctas as
+ * kq_ldlq_step_encode (uniform-K launches only).
  */
-int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int K, const uint16_t* labels, int tailbite_ctx,
-                       int max_ctas, void* workspace, size_t workspace_bytes, void* stream);
+int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int tailbite_ctx, int max_ctas, void* workspace,
+                       size_t workspace_bytes, void* stream);
 
 /*
  * Pack the low K bits of every state into 16*K uint16 words per tile in the

@@ -50,7 +50,8 @@ class ChainItem(ctypes.Structure):
     _fields_ = [("W", ctypes.c_void_p), ("P", ctypes.c_void_p), ("L", ctypes.c_void_p), ("err", ctypes.c_void_p),
                 ("wq", ctypes.c_void_p), ("enc", ctypes.c_void_p), ("size_k", ctypes.c_int64),
                 ("size_n", ctypes.c_int64), ("r0", ctypes.c_int64), ("end", ctypes.c_int64),
-                ("tile_col0", ctypes.c_int64), ("n_tiles", ctypes.c_int64)]
+                ("tile_col0", ctypes.c_int64), ("n_tiles", ctypes.c_int64), ("labels", ctypes.c_void_p),
+                ("K", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 _lib = None
 _lock = threading.Lock()
@@ -89,7 +90,7 @@ def load() -> ctypes.CDLL:
         L.kq_bf16_to_f32_transposed.argtypes = [P, I64, I64, I64, P, P, P]
         L.kq_gemm_abt_tf32.argtypes = [P, P, P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_float, P, P]
         L.kq_ldlq_step_encode.argtypes = [P, P, I64, I64, I64, I64, I, P, I, P, P, P, I, P, SZ, P]
-        L.kq_ldlq_chain_step.argtypes = [P, I, I, P, I, I, P, SZ, P]
+        L.kq_ldlq_chain_step.argtypes = [P, I, I, I, P, SZ, P]
         L.kq_hessian_workspace_bytes.argtypes = [I64, I64, I]
         L.kq_hessian_workspace_bytes.restype = SZ
         L.kq_accumulate_hessian.argtypes = [P, P, I64, I64, I64, P, I64, I, P, SZ, P, P]
@@ -423,24 +424,23 @@ def ldlq_step_encode(W: torch.Tensor, comp: torch.Tensor, r0: int, K: int, label
     stats.launches += 1
 
 
-def ldlq_chain_step(items, K: int, labels: torch.Tensor, tailbite_context: int, device: torch.device,
-                    max_ctas: int = 0) -> None:
-    """One launch of LDLQ chain steps; ``items`` is a sequence of ChainItem (at most KQ_CHAIN_MAX_ITEMS)."""
+def ldlq_chain_step(items, tailbite_context: int, device: torch.device, max_ctas: int = 0) -> None:
+    """One launch of LDLQ chain steps; ``items`` is a sequence of ChainItem (at most KQ_CHAIN_MAX_ITEMS), each
+    with its own K and label table (items of different K: one wave, even item starts)."""
     n = len(items)
     if not 1 <= n <= KQ_CHAIN_MAX_ITEMS:
         raise ValueError(f"ldlq_chain_step: 1..{KQ_CHAIN_MAX_ITEMS} items")
     arr = (ChainItem * n)(*items)
     tiles = sum(int(it.n_tiles) for it in items)
     with torch.cuda.device(device):
-        need = viterbi_workspace_bytes(K, tiles)
+        need = viterbi_workspace_bytes(3, tiles)
         ws = workspace(device, need)
         if stats.timing:
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record()
-        _check(load().kq_ldlq_chain_step(ctypes.cast(arr, ctypes.c_void_p), n, int(K), labels.data_ptr(),
-                                         int(tailbite_context), int(max_ctas), ws.data_ptr(), ws.numel(),
-                                         _stream(device)), "kq_ldlq_chain_step")
+        _check(load().kq_ldlq_chain_step(ctypes.cast(arr, ctypes.c_void_p), n, int(tailbite_context), int(max_ctas),
+                                         ws.data_ptr(), ws.numel(), _stream(device)), "kq_ldlq_chain_step")
         if stats.timing:
             b.record()
             stats.events.append((a, b, tiles, int(tailbite_context)))

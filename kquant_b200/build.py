@@ -37,7 +37,7 @@ def _stale() -> bool:
     if not LIB.exists():
         return True
     t = LIB.stat().st_mtime
-    deps = sources() + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "kq_b200.h", Path(__file__)]
+    deps = sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.inc")) + [ROOT / "include" / "kq_b200.h", Path(__file__)]
     return any(p.stat().st_mtime > t for p in deps)
 
 

@@ -21,6 +21,7 @@
 //    one another, and a job's traceback phase (C or 256 steps) never
 //    outlasts the other job's forward phase (2C or 256 steps), so the stagger
 //    keeps the ALU busy without a second buffer.
+#include <algorithm>
 #include "kq_viterbi_common.cuh"
 
 namespace kq {
@@ -361,299 +362,45 @@ __host__ __device__ constexpr size_t pair_smem_bytes() {
            kJobs * 2 * 4;
 }
 
+// The kernel body for one K; dec_base is this CTA's decision area
+// (kJobs x 256 rows of PairMap<K>::ROW_BYTES).  The single-K kernels hold the
+// body inline; the mixed-K chain kernel calls this device copy per CTA.
+template <int K, class IO>
+__device__ __forceinline__ void pair_body(const IO& io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
+                                          const __half* __restrict__ labels16, int C, int njobs,
+                                          uint8_t* __restrict__ dec_base)
+{
+#include "kq_viterbi_pair_body.inc"
+}
+
 template <int K, class IO>
 __global__ void __launch_bounds__(kThreads, 1)
 pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
             const __half* __restrict__ labels16, int C, int njobs, uint8_t* __restrict__ decisions)
 {
-    using M = PairMap<K>;
-    extern __shared__ __align__(16) uint8_t smem[];
-    // One (A, B) cost double buffer shared by the jobs: forward phases are
-    // non-preemptive, so at most one job is between forward steps at a time.
-    half2* cost = reinterpret_cast<half2*>(smem);                       // [2][NODES]
-    half2* wsh = cost + 2 * M::NODES;                                   // [kJobs][256] (A, B)
-    uint16_t* enc = reinterpret_cast<uint16_t*>(wsh + kJobs * 256);     // [kJobs][2][256]
-    uint32_t* red = reinterpret_cast<uint32_t*>(enc + kJobs * 2 * 256); // [kJobs][2][16]
-    int* es_sh = reinterpret_cast<int*>(red + kJobs * 2 * 16);          // [kJobs][2]
-    float* stage = reinterpret_cast<float*>(smem + ((pair_smem_bytes<K>() + 15) & ~(size_t)15));   // IO staging
+    uint8_t* dec_base = decisions + (size_t)blockIdx.x * kJobs * 256 * PairMap<K>::ROW_BYTES;
+#include "kq_viterbi_pair_body.inc"
+}
 
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
-    const int64_t n_pairs = (n_tiles + 1) >> 1;
-    const bool tb_lane = (warp == 0) && (lane < 2 * kJobs);
-    const int tb_job = (lane >> 1) & (kJobs - 1), tb_tile = lane & 1;
+// Decision row bytes of the widest K (K2 and K3: 8 KiB).
+constexpr size_t kMaxRowBytes =
+    PairMap<2>::ROW_BYTES > PairMap<3>::ROW_BYTES
+        ? (PairMap<2>::ROW_BYTES > PairMap<4>::ROW_BYTES ? PairMap<2>::ROW_BYTES : PairMap<4>::ROW_BYTES)
+        : (PairMap<3>::ROW_BYTES > PairMap<4>::ROW_BYTES ? PairMap<3>::ROW_BYTES : PairMap<4>::ROW_BYTES);
 
-    half2 L[M::G][M::PB][M::Q];
-#pragma unroll
-    for (int g = 0; g < M::G; ++g)
-#pragma unroll
-        for (int p = 0; p < M::PB; ++p)
-#pragma unroll
-            for (int k = 0; k < M::Q; ++k) {
-                const uint32_t t = ((uint32_t)k << (16 - K)) | (uint32_t)(M::base(tid, g) + 2 * p);
-                const uint32_t v = __ldg(labels32 + (t >> 1));
-                L[g][p][k] = *reinterpret_cast<const half2*>(&v);
-            }
-
-    uint8_t* dec_base = decisions + (size_t)blockIdx.x * kJobs * 256 * M::ROW_BYTES;
-    auto dec_job = [&](int j) { return dec_base + (size_t)j * 256 * M::ROW_BYTES; };
-    auto load_pair = [&](int j, int64_t q) {
-        const int t = tid >> 8, r = tid & 255;
-        int64_t tile = 2 * q + t;
-        if (tile >= n_tiles) tile = 2 * q;
-        float v;
-        if constexpr (IO::kStageFloats > 0) {
-            const int64_t tB = (2 * q + 1 < n_tiles) ? 2 * q + 1 : 2 * q;
-            v = io.load_staged(2 * q, tB, t, r, stage, tid);
-        } else {
-            v = io.load(tile, r);
-        }
-        reinterpret_cast<__half*>(wsh + j * 256 + r)[t] = __float2half_rn(v);
-    };
-
-    int phase[kJobs], step[kJobs], par[kJobs];
-    int64_t pair[kJobs];
-    int64_t taken = 0;
-    TbLane tb{0, 0};
-#pragma unroll
-    for (int j = 0; j < kJobs; ++j) {
-        const int64_t q = (int64_t)blockIdx.x + (int64_t)gridDim.x * taken;
-        pair[j] = q;
-        step[j] = 0;
-        par[j] = 0;
-        if (j < njobs && q < n_pairs) {
-            phase[j] = PH_FP;
-            ++taken;
-            load_pair(j, q);
-        } else {
-            phase[j] = PH_IDLE;
-        }
-    }
-    __syncthreads();
-
-    while (true) {
-        bool any = false, ctrl = false;
-#pragma unroll
-        for (int j = 0; j < kJobs; ++j) {
-            any |= (phase[j] != PH_IDLE);
-            ctrl |= (phase[j] == PH_AM) || (phase[j] == PH_OUT);
-        }
-        if (!any) break;
-
-        if (ctrl) {
-            // Control slot: primer argmin and tile output / refill.
-            int64_t qnext[kJobs];
-            int64_t cnt = taken;
-#pragma unroll
-            for (int j = 0; j < kJobs; ++j) {
-                qnext[j] = n_pairs;
-                if (phase[j] == PH_OUT) {
-                    const int64_t q = (int64_t)blockIdx.x + (int64_t)gridDim.x * cnt;
-                    if (q < n_pairs) { qnext[j] = q; ++cnt; }
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < kJobs; ++j) {
-                if (phase[j] == PH_AM) {
-                    // Argmin over the second-to-last primer step (the reference's buffer quirk).
-                    const half2* c = cost + (par[j] ^ 1) * M::NODES;
-                    uint32_t bA = 0xFFFFFFFFu, bB = 0xFFFFFFFFu;
-#pragma unroll
-                    for (int g = 0; g < M::G; ++g)
-#pragma unroll
-                        for (int q = 0; q < 2 * M::PB; ++q) {
-                            const int e = M::base(tid, g) + q;
-                            const uint32_t bits = *reinterpret_cast<const uint32_t*>(c + e);
-                            const uint32_t key = tie_key<K>(e);
-                            bA = min(bA, (bits << 16) | key);
-                            bB = min(bB, (bits & 0xFFFF0000u) | key);
-                        }
-                    bA = __reduce_min_sync(0xFFFFFFFFu, bA);
-                    bB = __reduce_min_sync(0xFFFFFFFFu, bB);
-                    if (lane == 0) {
-                        red[(j * 2 + 0) * 16 + warp] = bA;
-                        red[(j * 2 + 1) * 16 + warp] = bB;
-                    }
-                } else if (phase[j] == PH_OUT) {
-                    const int t = tid >> 8, r = tid & 255;
-                    const int64_t tile = 2 * pair[j] + t;
-                    if (tile < n_tiles) {
-                        const uint16_t sv = enc[(j * 2 + t) * 256 + r];
-                        io.store(tile, r, sv, __half2float(labels16[sv]));
-                    }
-                    if (qnext[j] < n_pairs) load_pair(j, qnext[j]);
-                }
-            }
-            __syncthreads();
-#pragma unroll
-            for (int j = 0; j < kJobs; ++j) {
-                if (phase[j] == PH_AM) {
-                    phase[j] = PH_TP;
-                    step[j] = 0;
-                    if (tb_lane && tb_job == j) {
-                        uint32_t best = 0xFFFFFFFFu;
-                        for (int w = 0; w < kThreads / 32; ++w) best = min(best, red[(j * 2 + tb_tile) * 16 + w]);
-                        tb.node = key_node<K>(best & 0xFFFFu);
-                        tb.row = C - 1;
-                    }
-                } else if (phase[j] == PH_OUT) {
-                    if (qnext[j] < n_pairs) { pair[j] = qnext[j]; ++taken; phase[j] = PH_FP; }
-                    else phase[j] = PH_IDLE;
-                    step[j] = 0;
-                    par[j] = 0;
-                }
-            }
-            continue;
-        }
-
-        // Forward job: a job inside a forward phase keeps it (the cost buffer is
-        // shared); otherwise the ready job with the shortest phase goes first.
-        int F = -1, F_rem = 0, F_key = 1 << 30;
-#pragma unroll
-        for (int j = 0; j < kJobs; ++j) {
-            if (phase[j] == PH_FP || phase[j] == PH_FF) {
-                const int rem = (phase[j] == PH_FP ? 2 * C : 256) - step[j];
-                const int key = step[j] > 0 ? -1 : rem;
-                if (key < F_key) { F_key = key; F_rem = rem; F = j; }
-            }
-        }
-        static_assert(kJobs == 2, "job selection below assumes two jobs");
-        const int my_phase = tb_job ? phase[1] : phase[0];
-        const int my_step = tb_job ? step[1] : step[0];
-        const bool my_tb = tb_lane && (my_phase == PH_TP || my_phase == PH_TF);
-        const uint8_t* my_dec = dec_job(tb_job);
-        uint16_t* my_enc = enc + (tb_job * 2 + tb_tile) * 256;
-
-        if (F < 0) {
-            // Every active job is in a traceback phase and every thread is idle.
-            // The cost buffer holds nothing live (the next forward step of any
-            // job starts from virtual costs), so it stages chunks of decision
-            // rows: all threads copy the next rows of each job with coalesced
-            // 16-byte loads, then the traceback lanes walk them from shared
-            // memory instead of paying one dependent global load per step.
-            int rem0 = 0, rem1 = 0, row0 = 0, row1 = 0;
-            if (phase[0] == PH_TP) { rem0 = C - step[0]; row0 = C - 1 - step[0]; }
-            if (phase[0] == PH_TF) { rem0 = 256 - step[0]; row0 = 255 - step[0]; }
-            if (phase[1] == PH_TP) { rem1 = C - step[1]; row1 = C - 1 - step[1]; }
-            if (phase[1] == PH_TF) { rem1 = 256 - step[1]; row1 = 255 - step[1]; }
-            const int ntb = (rem0 > 0) + (rem1 > 0);
-            // Rows stream through kStageBufs buffers with cp.async, kStageBufs - 1
-            // chunks in flight while the lanes walk the oldest: the copy runs at
-            // memory bandwidth instead of one latency-bound chunk at a time.
-            const int cap = (2 * M::NODES * 4) / (ntb * M::ROW_BYTES * kStageBufs);   // rows per job per buffer
-            const int nchunks = (max(rem0, rem1) + cap - 1) / cap;
-            uint8_t* stage = reinterpret_cast<uint8_t*>(cost);
-            const size_t buf_bytes = (size_t)ntb * cap * M::ROW_BYTES;
-            const int slot_of1 = (rem0 > 0) ? 1 : 0;                     // job 1's slot in a buffer
-            auto issue = [&](int c) {
-                if (c < nchunks) {
-                    uint8_t* buf = stage + (size_t)(c % kStageBufs) * buf_bytes;
-#pragma unroll
-                    for (int j = 0; j < kJobs; ++j) {
-                        const int rem = j ? rem1 : rem0, top = j ? row1 : row0;
-                        const int lo = c * cap, R = min(cap, rem - lo);
-                        if (R <= 0) continue;
-                        const uint8_t* src = dec_job(j) + (size_t)(top - lo - R + 1) * M::ROW_BYTES;
-                        uint8_t* dst = buf + (size_t)(j ? slot_of1 : 0) * cap * M::ROW_BYTES;
-                        const int units = R * M::ROW_BYTES / 16;
-                        for (int i = tid; i < units; i += kThreads) {
-                            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                         ::"r"((uint32_t)__cvta_generic_to_shared(dst + 16 * i)), "l"(src + 16 * i)
-                                         : "memory");
-                        }
-                    }
-                }
-                asm volatile("cp.async.commit_group;" ::: "memory");
-            };
-#pragma unroll
-            for (int c = 0; c < kStageBufs - 1; ++c) issue(c);
-            for (int c = 0; c < nchunks; ++c) {
-                issue(c + kStageBufs - 1);
-                asm volatile("cp.async.wait_group %0;" ::"n"(kStageBufs - 1) : "memory");
-                __syncthreads();
-                if (my_tb) {
-                    const int rem = tb_job ? rem1 : rem0, top = tb_job ? row1 : row0;
-                    const int lo = c * cap, R = min(cap, rem - lo);
-                    const int first = top - lo - R + 1;
-                    const uint8_t* sl = stage + (size_t)(c % kStageBufs) * buf_bytes +
-                                        (size_t)(tb_job ? slot_of1 : 0) * cap * M::ROW_BYTES;
-                    for (int s2 = 0; s2 < R; ++s2) {
-                        int owner, word, sh;
-                        M::locate(tb.node, tb_tile, owner, word, sh);
-                        const unsigned int w = reinterpret_cast<const unsigned int*>(
-                            sl + (size_t)(tb.row - first) * M::ROW_BYTES + (size_t)owner * M::WORD_BYTES)[word];
-                        const int d = (int)((w >> sh) & (M::Q - 1));
-                        if (my_phase == PH_TF) my_enc[tb.row] = (uint16_t)((d << (16 - K)) | tb.node);
-                        tb.node = (d << M::DSHIFT) | (tb.node >> K);
-                        --tb.row;
-                    }
-                }
-                __syncthreads();
-            }
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-            if (my_tb && my_phase == PH_TP) {
-                es_sh[tb_job * 2 + tb_tile] = tb.node;
-                tb.row = 255;
-            }
-            __syncthreads();
-#pragma unroll
-            for (int j = 0; j < kJobs; ++j) {
-                if (phase[j] == PH_TP) { phase[j] = PH_FF; step[j] = 0; }
-                else if (phase[j] == PH_TF) { phase[j] = PH_OUT; step[j] = 0; }
-            }
-            continue;
-        }
-
-        const int ph = F ? phase[1] : phase[0];
-        const int i0 = F ? step[1] : step[0];
-        int S = F_rem;
-        if (ph == PH_FP && i0 < C) S = C - i0;           // decision-free part of the primer
-        if (i0 == 0) S = 1;                               // step 0 has its own variant
-#pragma unroll
-        for (int j = 0; j < kJobs; ++j) {
-            if (j != F && phase[j] == PH_TP) S = min(S, C - step[j]);
-            if (j != F && phase[j] == PH_TF) S = min(S, 256 - step[j]);
-        }
-        const int ri0 = (ph == PH_FP) ? ((i0 + 256 - C) & 255) : i0;
-        const bool run_tb = my_tb && (tb_job != F);
-        const bool tb_final = (my_phase == PH_TF);
-        half2* cj = cost;
-        int pF = F ? par[1] : par[0];
-        if (i0 == 0) {
-            if (ph == PH_FP)
-                run_steps<K, false, 1>(L, cj, pF, wsh + F * 256, ri0, S, 0, 0, dec_job(F), tid, run_tb, tb_final, tb,
-                                       my_dec, tb_tile, my_enc);
-            else
-                run_steps<K, true, 2>(L, cj, pF, wsh + F * 256, ri0, S, es_sh[F * 2], es_sh[F * 2 + 1], dec_job(F),
-                                      tid, run_tb, tb_final, tb, my_dec, tb_tile, my_enc);
-        } else if (ph == PH_FF || i0 >= C) {
-            run_steps<K, true, 0>(L, cj, pF, wsh + F * 256, ri0, S, 0, 0, dec_job(F), tid, run_tb, tb_final, tb,
-                                  my_dec, tb_tile, my_enc);
-        } else {
-            run_steps<K, false, 0>(L, cj, pF, wsh + F * 256, ri0, S, 0, 0, dec_job(F), tid, run_tb, tb_final, tb,
-                                   my_dec, tb_tile, my_enc);
-        }
-        // Chains that finished their primer traceback publish the end state.
-        if (run_tb && my_phase == PH_TP && my_step + S == C) {
-            es_sh[tb_job * 2 + tb_tile] = tb.node;
-            tb.row = 255;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < kJobs; ++j) {
-            if (j == F) {
-                par[j] = pF;
-                step[j] += S;
-                if (phase[j] == PH_FP && step[j] == 2 * C) { phase[j] = PH_AM; step[j] = 0; }
-                else if (phase[j] == PH_FF && step[j] == 256) { phase[j] = PH_TF; step[j] = 0; }
-            } else if (phase[j] == PH_TP) {
-                step[j] += S;
-                if (step[j] == C) { phase[j] = PH_FF; step[j] = 0; }
-            } else if (phase[j] == PH_TF) {
-                step[j] += S;
-                if (step[j] == 256) { phase[j] = PH_OUT; step[j] = 0; }
-            }
-        }
+// Chain launch whose items may differ in K: one tile pair per CTA (a single
+// wave), each CTA running the body for its pair's K with that item's labels.
+__global__ void __launch_bounds__(kThreads, 1)
+pair_kernel_mk(const __grid_constant__ ChainIO io, int64_t n_tiles, int C, uint8_t* __restrict__ decisions)
+{
+    const kq_chain_item& c = io.it[io.find(2 * (int64_t)blockIdx.x)];
+    uint8_t* dec = decisions + (size_t)blockIdx.x * kJobs * 256 * kMaxRowBytes;
+    const uint32_t* l32 = reinterpret_cast<const uint32_t*>(c.labels);
+    const __half* l16 = reinterpret_cast<const __half*>(c.labels);
+    switch (c.K) {
+    case 2: pair_body<2, ChainIO>(io, n_tiles, l32, l16, C, 1, dec); break;
+    case 3: pair_body<3, ChainIO>(io, n_tiles, l32, l16, C, 1, dec); break;
+    default: pair_body<4, ChainIO>(io, n_tiles, l32, l16, C, 1, dec); break;
     }
 }
 
@@ -794,31 +541,34 @@ extern "C" int kq_ldlq_step_encode(const float* W, const float* comp, int64_t ba
                             workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int K, const uint16_t* labels,
-                                  int tailbite_ctx, int max_ctas, void* workspace, size_t workspace_bytes,
-                                  void* stream) {
+extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int tailbite_ctx, int max_ctas,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
     using namespace kq;
-    if (!items || n_items < 1 || n_items > KQ_CHAIN_MAX_ITEMS || !labels) {
-        set_error("kq_ldlq_chain_step: need 1..%d items and labels (got %d)", KQ_CHAIN_MAX_ITEMS, n_items);
+    if (!items || n_items < 1 || n_items > KQ_CHAIN_MAX_ITEMS) {
+        set_error("kq_ldlq_chain_step: need 1..%d items (got %d)", KQ_CHAIN_MAX_ITEMS, n_items);
         return KQ_ERR_ARG;
     }
     if (tailbite_ctx < 1 || tailbite_ctx > 128) {
         set_error("tailbite_context must be in 1..128 (got %d)", tailbite_ctx);
         return KQ_ERR_ARG;
     }
-    if (((uintptr_t)labels & 3) || ((uintptr_t)workspace & 15)) {
-        set_error("kq_ldlq_chain_step: labels must be 4-byte and workspace 16-byte aligned");
+    if ((uintptr_t)workspace & 15) {
+        set_error("kq_ldlq_chain_step: workspace must be 16-byte aligned");
         return KQ_ERR_ALIGN;
     }
     ChainIO io;
     io.n = n_items;
     int64_t total = 0;
+    bool mixed = false, even = true;
+    int kmask = 0;
     for (int i = 0; i < n_items; ++i) {
         const kq_chain_item& c = items[i];
-        if (!c.W || !c.P || !c.L || !c.err || !c.wq || !c.enc) {
+        if (!c.W || !c.P || !c.L || !c.err || !c.wq || !c.enc || !c.labels) {
             set_error("kq_ldlq_chain_step: item %d has a null pointer", i);
             return KQ_ERR_ARG;
         }
+        if (c.K < 2 || c.K > 4) { set_error("kq_ldlq_chain_step: item %d has K=%d", i, c.K); return KQ_ERR_ARG; }
+        if ((uintptr_t)c.labels & 3) { set_error("kq_ldlq_chain_step: labels must be 4-byte aligned"); return KQ_ERR_ALIGN; }
         if (c.size_k <= 0 || c.size_n <= 0 || c.size_k % 16 || c.size_n % 16 || c.r0 < 0 || c.r0 % 16 ||
             c.end < c.r0 + 16 || c.end > c.size_k || c.n_tiles <= 0 || c.tile_col0 < 0 ||
             c.tile_col0 + c.n_tiles > c.size_n / 16) {
@@ -827,11 +577,38 @@ extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int K
                       (long long)c.tile_col0, (long long)c.n_tiles);
             return KQ_ERR_ARG;
         }
+        mixed |= c.K != items[0].K;
+        even &= (total % 2) == 0;
+        kmask |= 1 << c.K;
         io.it[i] = c;
         io.start[i] = total;
         total += c.n_tiles;
     }
     io.start[n_items] = total;
-    return ldlq_step_encode(io, total, K, labels, tailbite_ctx, max_ctas, static_cast<uint8_t*>(workspace),
-                            workspace_bytes, static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!mixed)
+        return ldlq_step_encode(io, total, items[0].K, items[0].labels, tailbite_ctx, max_ctas,
+                                static_cast<uint8_t*>(workspace), workspace_bytes, s);
+    int sms = 0;
+    if (int rc = sm_count(&sms)) return rc;
+    const int64_t pairs = (total + 1) / 2;
+    if (pairs > sms || !even) {
+        set_error("kq_ldlq_chain_step: items of different K need one wave (%lld pairs > %d SMs) and even item starts",
+                  (long long)pairs, sms);
+        return KQ_ERR_ARG;
+    }
+    const size_t need = (size_t)pairs * kJobs * 256 * kMaxRowBytes;
+    if (workspace_bytes < need) {
+        set_error("viterbi workspace too small: %zu < %zu", workspace_bytes, need);
+        return KQ_ERR_WORKSPACE;
+    }
+    size_t sm = 0;
+    if (kmask & 4) sm = std::max(sm, pair_smem_bytes<2>());
+    if (kmask & 8) sm = std::max(sm, pair_smem_bytes<3>());
+    if (kmask & 16) sm = std::max(sm, pair_smem_bytes<4>());
+    sm = ((sm + 15) & ~(size_t)15) + (size_t)ChainIO::kStageFloats * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(pair_kernel_mk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
+    pair_kernel_mk<<<(int)pairs, kThreads, sm, s>>>(io, total, tailbite_ctx, static_cast<uint8_t*>(workspace));
+    return check_launch("pair_kernel_mk");
 }

@@ -787,6 +787,18 @@ def ldlq_mixed_batched(weights, Ls, quant_args_list, pb=None, *, synchronize=Tru
             raise ValueError("mixed LDLQ continuation state has invalid shape or type")
         state = (initial_weights_q, initial_encoded_q, initial_product_cache)
     del prepared_groupings  # the rate plan below is built once per call and cached per step key
+    if (state is None and source_indices is None and process_begin == 0 and process_end == size_k
+            and len(devices) == 1):
+        wq = torch.empty((B, size_k, size_n), dtype=weights.dtype, device=weights.device)
+        enc = torch.empty((B, size_k // 16, size_n // 16, 256), dtype=torch.int16, device=weights.device)
+        P = torch.zeros_like(wq)
+        with torch.cuda.stream(get_quant_stream(devices[0])):
+            members = [_ChainMember(weights[b], Ls[b], wq[b], enc[b], quant_args_list[b], rate=(axis, bits),
+                                    P=P[b]) for b, (_, bits) in enumerate(normalized)]
+            _chain_traverse(members, weights.device)
+        if synchronize:
+            _sync(devices)
+        return (wq, enc, P) if return_product_cache else (wq, enc)
     plan = _RatePlan([bits for _, bits in normalized], axis, B, size_n // 16, weights.device)
     with torch.cuda.stream(get_quant_stream(devices[0])):
         wq, enc, P = _ldlq_traverse(weights, Ls, quant_args_list[0], plan, buffer_rows=rows, tf32=tf32,
@@ -822,8 +834,7 @@ def ldlq_mixed_n_candidates_reuse(weights: torch.Tensor, Ls: torch.Tensor, quant
         if norm[0][1] != (3,) * (size_n // 16):
             raise ValueError("output-axis reuse requires an all-K3 first candidate")
         maps.append([bits for _, bits in norm])
-    base_wq, base_enc = ldlq_mixed_batched(weights, Ls, [g[0] for g in quant_args_groups])
-
+    dev = weights.device
     specs = []
     for s, cand in enumerate(maps):
         width = {}
@@ -837,24 +848,28 @@ def ldlq_mixed_n_candidates_reuse(weights: torch.Tensor, Ls: torch.Tensor, quant
             pos = tuple(t for t, x in width.items() if x == w)
             if pos:
                 specs.append((s, w, pos))
-    dev = weights.device
 
     def cols(tiles):
         return torch.tensor([c for t in tiles for c in range(16 * t, 16 * t + 16)], dtype=torch.int64, device=dev)
 
+    # The all-K3 base of every source and the K2 / K4 replacement columns are
+    # independent LDLQ problems (columns do not couple): one chain-engine run.
+    devices = quant_args_groups[0][0]["devices"]
+    _sync(devices)
+    base_wq = torch.empty_like(weights)
+    base_enc = torch.empty((S, size_k // 16, size_n // 16, 256), dtype=torch.int16, device=dev)
     overrides = {}
-    for count in sorted({len(p) for _, _, p in specs}):
-        members = [sp for sp in specs if len(sp[2]) == count]
-        mw = torch.stack([weights[s].index_select(1, cols(pos)) for s, _, pos in members])
-        mL = torch.stack([Ls[s] for s, _, _ in members])
-        margs = []
-        for s, w, _ in members:
-            a = dict(quant_args_groups[s][0])
-            a["mixed_tile_bits"] = (w,) * count
-            margs.append(a)
-        owq, oenc = ldlq_mixed_batched(mw, mL, margs)
-        for i, (s, w, pos) in enumerate(members):
-            overrides[(s, w)] = (pos, owq[i], oenc[i])
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        members = [_ChainMember(weights[s], Ls[s], base_wq[s], base_enc[s], quant_args_groups[s][0], rate=3)
+                   for s in range(S)]
+        for s, w, pos in specs:
+            sub = weights[s].index_select(1, cols(pos)).contiguous()
+            owq = torch.empty_like(sub)
+            oenc = torch.empty((size_k // 16, len(pos), 256), dtype=torch.int16, device=dev)
+            members.append(_ChainMember(sub, Ls[s], owq, oenc, quant_args_groups[s][0], rate=w))
+            overrides[(s, w)] = (pos, owq, oenc)
+        _chain_traverse(members, dev)
+    _sync(devices)
 
     out_wq, out_enc = [], []
     for s, cand in enumerate(maps):
@@ -896,64 +911,99 @@ def ldlq_mixed_k_candidates_prefix_reuse(weights: torch.Tensor, Ls: torch.Tensor
         raise ValueError("input-axis prefix reuse needs candidates for every source")
     if not any(len(g) > 1 for g in quant_args_groups):
         raise ValueError("input-axis prefix reuse needs at least one multi-candidate source")
-    maps, starts = [], []
+    maps = []
     for group in quant_args_groups:
         norm = [mixed_rate_spec(size_k, size_n, a) for a in group]
         if any(ax != "k" for ax, _ in norm):
             raise ValueError("input-axis prefix reuse supports only mixed_rate_axis='k'")
-        m = [bits for _, bits in norm]
-        start = len(m[0])
-        while start > 0 and len({bits[start - 1] for bits in m}) == 1:
-            start -= 1
-        maps.append(m)
-        starts.append(start)
+        maps.append([bits for _, bits in norm])
     rows = max(quant_args_groups[0][0].get("buf_size_k", 128), 16)
     if any(max(a.get("buf_size_k", 128), 16) != rows for g in quant_args_groups for a in g):
         raise ValueError("input-axis prefix reuse requires one LDLQ buffer size")
-    split = -(-max(starts) * 16 // rows) * rows
+    if rows % 16 or size_k % rows:
+        raise ValueError("input-axis prefix reuse buffer must tile the EXL K dimension")
     flat = [(s, c) for s, g in enumerate(quant_args_groups) for c in range(len(g))]
     dev = weights.device
-    if split >= size_k:
-        return ldlq_mixed_batched(torch.stack([weights[s] for s, _ in flat]), torch.stack([Ls[s] for s, _ in flat]),
-                                  [quant_args_groups[s][c] for s, c in flat])
-    wq, enc, P = ldlq_mixed_batched(weights, Ls, [g[0] for g in quant_args_groups], process_begin=split,
-                                    process_end=size_k, return_product_cache=True)
-    if split == 0:
-        src = torch.tensor([s for s, _ in flat], dtype=torch.long, device=dev)
-        return wq.index_select(0, src), enc.index_select(0, src)
-    nodes = [(s, tuple(range(len(g)))) for s, g in enumerate(quant_args_groups)]
     devices = quant_args_groups[0][0]["devices"]
-    with torch.cuda.stream(get_quant_stream(devices[0])):
-        for end in range(split, 0, -rows):
-            begin = end - rows
-            t0, t1 = begin // 16, end // 16
-            children, parents, args = [], [], []
-            for parent, (s, cands) in enumerate(nodes):
-                parts: dict = {}
-                for c in cands:
-                    parts.setdefault(maps[s][c][t0:t1], []).append(c)
-                for members in parts.values():
-                    children.append((s, tuple(members)))
-                    parents.append(parent)
-                    args.append(quant_args_groups[s][members[0]])
-            if len(children) != len(nodes) or any(p != i for i, p in enumerate(parents)):
-                pidx = torch.tensor(parents, dtype=torch.long, device=dev)
-                wq, enc, P = wq.index_select(0, pidx), enc.index_select(0, pidx), P.index_select(0, pidx)
-            nodes = children
-            srcs = torch.tensor([s for s, _ in nodes], dtype=torch.long, device=dev)
-            wq, enc, P = ldlq_mixed_batched(weights, Ls, args, synchronize=False, process_begin=begin,
-                                            process_end=end, initial_weights_q=wq, initial_encoded_q=enc,
-                                            initial_product_cache=P, return_product_cache=True,
-                                            source_indices=srcs)
-    _sync(devices)
-    where = {}
-    for i, (s, cands) in enumerate(nodes):
+    # Trie of LDLQ states as chain-engine members: a node holds the candidates
+    # whose maps agree on every buffer traversed so far; when one of its chains
+    # reaches a buffer where they differ, the node splits.  The part holding
+    # the node's representative candidate keeps its arrays; every other part
+    # gets fresh ones, filled column slice by column slice as the node's
+    # chains arrive, and continues from the same row.
+    node = {}                                   # id(member) -> [source, candidates, representative]
+
+    def new_member(s, cands, like=None):
+        qa = quant_args_groups[s][cands[0]]
+        rate = ("k", maps[s][cands[0]])
+        if like is None:
+            m = _ChainMember(weights[s], Ls[s], torch.empty((size_k, size_n), dtype=weights.dtype, device=dev),
+                             torch.empty((size_k // 16, size_n // 16, 256), dtype=torch.int16, device=dev), qa,
+                             rate=rate)
+        else:
+            m = _ChainMember(like.W, like.L, torch.empty_like(like.wq), torch.empty_like(like.enc), qa, rate=rate,
+                             P=torch.empty_like(like.P), E=torch.empty_like(like.E))
+        node[id(m)] = [s, tuple(cands), cands[0]]
+        return m
+
+    def partition(s, cands, begin, end):
+        parts: dict = {}
         for c in cands:
-            where[(s, c)] = i
-    if set(where) != set(flat):
-        raise AssertionError("input-axis prefix trie lost a rate candidate")
-    out = torch.tensor([where[m] for m in flat], dtype=torch.long, device=dev)
-    return wq.index_select(0, out), enc.index_select(0, out)
+            parts.setdefault(maps[s][c][begin // 16:end // 16], []).append(c)
+        return list(parts.values())
+
+    forks: dict = {}
+
+    def on_buffer(chain):
+        m = chain.m
+        r0, end = chain.steps[chain.pos]
+        key = (id(m), end)
+        if key not in forks:
+            s, cands, rep = node[id(m)]
+            parts = partition(s, cands, end - rows, end)
+            if len(parts) == 1:
+                forks[key] = None
+            else:
+                children = []
+                for part in parts:
+                    if rep in part:
+                        node[id(m)][1] = tuple(part)
+                    else:
+                        children.append(new_member(s, part, like=m))
+                forks[key] = children
+        children = forks[key]
+        if not children:
+            return None
+        cs = slice(16 * chain.tile_col0, 16 * (chain.tile_col0 + chain.n_tiles))
+        ts = slice(chain.tile_col0, chain.tile_col0 + chain.n_tiles)
+        out = [chain]
+        for child in children:
+            child.wq[:, cs] = m.wq[:, cs]
+            child.enc[:, ts] = m.enc[:, ts]
+            child.P[:, cs] = m.P[:, cs]
+            child.E[:, cs] = m.E[:, cs]
+            out.append(_Chain(child, chain.tile_col0, chain.n_tiles, steps=chain.steps, pos=chain.pos))
+        return out
+
+    _sync(devices)
+    with torch.cuda.stream(get_quant_stream(devices[0])):
+        roots = [new_member(s, part) for s, g in enumerate(quant_args_groups)
+                 for part in partition(s, tuple(range(len(g))), size_k - rows, size_k)]
+        _chain_traverse(roots, dev, on_buffer=on_buffer)
+        members = {id(m): m for m in roots}
+        for children in forks.values():
+            for m in children or ():
+                members[id(m)] = m
+        where = {}
+        for mid, (s, cands, _) in node.items():
+            for c in cands:
+                where[(s, c)] = members[mid]
+        if set(where) != set(flat):
+            raise AssertionError("input-axis prefix trie lost a rate candidate")
+        wq = torch.stack([where[f].wq for f in flat])
+        enc = torch.stack([where[f].enc for f in flat])
+    _sync(devices)
+    return wq, enc
 
 
 def fallback_quant(weight: torch.Tensor, q_device, quant_args: dict, pb=None):
@@ -1742,51 +1792,87 @@ CHAIN_TILES = 32
 
 
 class _ChainMember:
-    """One [k, n] matrix of a chain-engine run with its LDLQ state."""
+    """One [k, n] matrix of a chain-engine run with its LDLQ state.
 
-    def __init__(self, W, L, wq, enc, quant_args):
+    ``rate`` gives the per-tile K: an int (uniform), ("n", bits per tile
+    column) or ("k", bits per tile row) as in mixed_rate_spec.  ``state``
+    optionally supplies (What, enc, P, E) arrays to fill instead of fresh ones.
+    """
+
+    def __init__(self, W, L, wq, enc, quant_args, rate=None, P=None, E=None):
         self.W = W
-        self.L = L.contiguous()
+        self.L = L if L.is_contiguous() else L.contiguous()
         self.wq = wq
         self.enc = enc
         self.k, self.n = W.shape
         assert W.is_contiguous() and wq.is_contiguous() and enc.is_contiguous()
         assert self.k % 16 == 0 and self.n % 16 == 0
-        self.P = torch.zeros_like(W)
-        self.E = torch.empty_like(W)
+        self.P = torch.zeros_like(W) if P is None else P
+        self.E = torch.empty_like(W) if E is None else E
         self.buffer_rows = _buffer_rows(quant_args, self.k)
         self.tf32 = bool(quant_args.get("ldlq_tf32", False))
-        bits = int(quant_args["K"])
-        if bits not in (2, 3, 4):
+        self.rate = int(quant_args["K"]) if rate is None else rate
+        bits = {self.rate} if isinstance(self.rate, int) else set(self.rate[1])
+        if not bits <= {2, 3, 4}:
             raise ValueError("the trellis kernel supports K2--K4")
-        ctx = int(quant_args.get("tailbite_context", 128))
-        if not 1 <= ctx <= 128:
+        self.ctx = int(quant_args.get("tailbite_context", 128))
+        if not 1 <= self.ctx <= 128:
             raise ValueError("tailbite_context must be in 1..128")
-        kind, lut = _tile_codebook(quant_args, bits)
-        self.labels = _labels_for(W.device, bits, kind, lut)
-        self.key = (bits, self.labels.data_ptr(), ctx)
+        self.labels = {}
+        for K in bits:
+            kind, lut = _tile_codebook(quant_args, K)
+            self.labels[K] = _labels_for(W.device, K, kind, lut)
+
+    def column_runs(self, width: int):
+        """Tile-column ranges of the chains: runs of one K along n, cut to at most ``width`` tiles."""
+        tn = self.n // 16
+        if isinstance(self.rate, tuple) and self.rate[0] == "n":
+            bits = self.rate[1]
+            runs, c0 = [], 0
+            for c in range(1, tn + 1):
+                if c == tn or bits[c] != bits[c0]:
+                    runs.append((c0, c))
+                    c0 = c
+        else:
+            runs = [(0, tn)]
+        out = []
+        for c0, c1 in runs:
+            out += [(c, min(width, c1 - c)) for c in range(c0, c1, width)]
+        return out
+
+    def bits_at(self, r0: int, tile_col: int) -> int:
+        if isinstance(self.rate, int):
+            return self.rate
+        axis, bits = self.rate
+        return bits[tile_col] if axis == "n" else bits[r0 // 16]
 
 
 class _Chain:
-    def __init__(self, member: _ChainMember, tile_col0: int, n_tiles: int):
+    def __init__(self, member: _ChainMember, tile_col0: int, n_tiles: int, steps=None, pos: int = 0):
         self.m = member
         self.tile_col0 = tile_col0
         self.n_tiles = n_tiles
         rows = member.buffer_rows
         # (r0, end) of every step, in traversal order (backward over 128-row buffers)
-        self.steps = [(end - rows + le - 16, end) for end in range(member.k, 0, -rows)
-                      for le in range(rows, 0, -16)]
-        self.pos = 0
+        self.steps = steps if steps is not None else [(end - rows + le - 16, end) for end in range(member.k, 0, -rows)
+                                                      for le in range(rows, 0, -16)]
+        self.pos = pos
 
     @property
     def remaining(self):
         return len(self.steps) - self.pos
 
+    @property
+    def K(self):
+        return self.m.bits_at(self.steps[self.pos][0], self.tile_col0)
+
     def item(self):
         m = self.m
         r0, end = self.steps[self.pos]
+        K = self.K
         return _native.ChainItem(m.W.data_ptr(), m.P.data_ptr(), m.L.data_ptr(), m.E.data_ptr(), m.wq.data_ptr(),
-                                 m.enc.data_ptr(), m.k, m.n, r0, end, self.tile_col0, self.n_tiles)
+                                 m.enc.data_ptr(), m.k, m.n, r0, end, self.tile_col0, self.n_tiles,
+                                 m.labels[K].data_ptr(), K, 0)
 
     def advance(self):
         """Step done: after a buffer's last step, P[:begin] += L[begin:end, :begin]^T E[begin:end] (own columns)."""
@@ -1804,44 +1890,56 @@ class _Chain:
                 torch.backends.cuda.matmul.allow_tf32 = previous
 
 
-def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None = None) -> None:
+def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None = None, on_buffer=None) -> None:
     """Block-LDLQ of every member (kquant/exl3_encoder_backend.py:389-505 per matrix), fills What and codes.
 
-    Each member splits into column chains of ``CHAIN_TILES`` tiles.  Every
-    launch (``kq_ldlq_chain_step``) advances a set of chains by one 16-row
-    step: the chains with the most steps left first (the critical path),
-    then any others that fit the launch's whole waves of 2 x SMs tiles,
-    all with the same (K, codebook, context).  The kernel computes each
-    step's feedback product itself; the buffer-end feedback updates run
-    between launches on the same stream.
+    Each member splits into column chains of at most ``CHAIN_TILES`` tiles
+    and one K along the output axis.  Every launch (``kq_ldlq_chain_step``)
+    advances a set of chains by one 16-row step: the chains with the most
+    steps left first (the critical path), then any others that fit one wave
+    of 2 x SMs tiles, all with the same tail-biting context; chains of
+    different K share launches.  The kernel computes each step's feedback
+    product itself; the buffer-end feedback updates run between launches on
+    the same stream.  ``on_buffer(chain)``, when given, is called when a chain
+    is about to start a new 128-row buffer and may return replacement chains
+    (the forks of a candidate trie).
     """
     width = chain_tiles or CHAIN_TILES
-    chains = []
-    for m in members:
-        tn = m.n // 16
-        for c0 in range(0, tn, width):
-            chains.append(_Chain(m, c0, min(width, tn - c0)))
+    chains = [_Chain(m, c0, nt) for m in members for c0, nt in m.column_runs(width)]
     cap = 2 * torch.cuda.get_device_properties(device).multi_processor_count
     order = {id(c): i for i, c in enumerate(chains)}
+    serial = len(chains)
     live = list(chains)
+    asked = set()
     while live:
+        if on_buffer is not None:
+            grown = []
+            for c in live:
+                r0, end = c.steps[c.pos]
+                if r0 == end - 16 and end < c.m.k and (id(c), c.pos) not in asked:
+                    asked.add((id(c), c.pos))
+                    new = on_buffer(c)
+                    if new:
+                        for n in new:
+                            order[id(n)] = serial
+                            serial += 1
+                        grown += new
+                        continue
+                grown.append(c)
+            live = grown
         live.sort(key=lambda c: (-c.remaining, order[id(c)]))
-        key = live[0].m.key
-        cand = [c for c in live if c.m.key == key]
+        ctx = live[0].m.ctx
         sel, tot = [], 0
-        for c in cand:
-            if len(sel) < _native.KQ_CHAIN_MAX_ITEMS and (tot + c.n_tiles <= cap or not sel):
-                sel.append(c)
-                tot += c.n_tiles
-        waves = -(-tot // cap)
-        for c in cand:
-            if c in sel or len(sel) >= _native.KQ_CHAIN_MAX_ITEMS:
+        for c in live:
+            if c.m.ctx != ctx or len(sel) >= _native.KQ_CHAIN_MAX_ITEMS:
                 continue
-            if tot + c.n_tiles <= waves * cap:
+            if tot + c.n_tiles <= cap or not sel:
                 sel.append(c)
                 tot += c.n_tiles
-        bits, _, ctx = key
-        _native.ldlq_chain_step([c.item() for c in sel], bits, sel[0].m.labels, ctx, device)
+        if len({c.K for c in sel}) > 1:
+            # different K share a launch only as one wave with pair-aligned items
+            sel.sort(key=lambda c: c.n_tiles % 2)
+        _native.ldlq_chain_step([c.item() for c in sel], ctx, device)
         for c in sel:
             c.advance()
         live = [c for c in live if c.remaining > 0]

@@ -219,3 +219,59 @@ def test_chain_engine_equals_cublas_feedback_path(cuda_device, B, k, n):
     torch.cuda.synchronize()
     assert torch.equal(enc_c, enc_s)
     assert torch.equal(wq_c, wq_s)
+
+
+def _mixed_case(dev, axis, seed):
+    k, n = 512, 256
+    ws, ls = [], []
+    for b in range(2):
+        w, h = _problem(dev, k=k, n=n, seed=seed + b)
+        L, _ = be.block_ldl(h.clone(), 16, {"devices": [str(dev)], "sigma_reg": 0.025}, False)
+        ws.append(w * 25)
+        ls.append(L)
+    return torch.stack(ws).contiguous(), torch.stack(ls).contiguous(), (n if axis == "n" else k) // 16
+
+
+def _old_path(W, Ls, qal):
+    """The unfused traversal (cuBLAS feedback, per-K tile launches): source_indices bypasses the chain engine."""
+    idx = torch.arange(W.shape[0], dtype=torch.long, device=W.device)
+    return be.ldlq_mixed_batched(W, Ls, qal, source_indices=idx)
+
+
+@pytest.mark.parametrize("axis", ["n", "k"])
+def test_mixed_chain_engine_equals_unfused_path(cuda_device, axis):
+    """Mixed-rate LDLQ on the chain engine (K2/K3/K4 chains sharing launches) == the unfused path."""
+    dev = cuda_device
+    W, Ls, nt = _mixed_case(dev, axis, 60)
+    maps = [tuple((2, 3, 4)[(i // 8 + b) % 3] for i in range(nt)) for b in range(2)]
+    qal = [_args(dev, mixed_rate_axis=axis, mixed_tile_bits=m) for m in maps]
+    wq_c, enc_c = be.ldlq_mixed_batched(W, Ls, qal)
+    wq_o, enc_o = _old_path(W, Ls, qal)
+    assert torch.equal(enc_c, enc_o)
+    assert torch.equal(wq_c, wq_o)
+
+
+@pytest.mark.parametrize("axis", ["n", "k"])
+def test_candidate_reuse_equals_independent_encodes(cuda_device, axis):
+    """n-axis reuse (base + replacement columns in one engine run) and k-axis prefix trie (forking chains) ==
+    every candidate encoded on its own by the unfused path."""
+    dev = cuda_device
+    W, Ls, nt = _mixed_case(dev, axis, 70)
+    base = tuple([3] * nt)
+    if axis == "n":
+        cands = [base, tuple([2] * 8 + [4] * 8 + [3] * (nt - 16)), tuple([2] * 8 + [3] * (nt - 8))]
+        reuse = be.ldlq_mixed_n_candidates_reuse
+    else:
+        # maps agree on the bottom buffers and diverge in the top two, in different buffers per candidate
+        cands = [base, tuple([2] * 8 + [4] * 8 + [3] * (nt - 16)), tuple([4] * 8 + [2] * 8 + [3] * (nt - 16)),
+                 tuple([3] * 8 + [2] * 4 + [4] * 4 + [3] * (nt - 16))]
+        reuse = be.ldlq_mixed_k_candidates_prefix_reuse
+    groups = [[_args(dev, mixed_rate_axis=axis, mixed_tile_bits=m) for m in cands] for _ in range(2)]
+    wq_r, enc_r = reuse(W, Ls, groups)
+    f = 0
+    for s in range(2):
+        for c in range(len(cands)):
+            wq_o, enc_o = _old_path(W[s:s + 1].contiguous(), Ls[s:s + 1].contiguous(), [groups[s][c]])
+            assert torch.equal(enc_r[f], enc_o[0]), (s, c)
+            assert torch.equal(wq_r[f], wq_o[0]), (s, c)
+            f += 1

@@ -13,26 +13,30 @@ from kquant_b200 import _native
 from kquant_b200 import exl3_encoder_backend as be
 
 
-class _Member:
-    def __init__(self, k, n, key, buffer_rows=128):
-        self.k, self.n = k, n
-        self.W = torch.empty((k, n), device="meta")
-        self.P = torch.empty((k, n), device="meta")
-        self.E = torch.empty((k, n), device="meta")
-        self.wq = torch.empty((k, n), device="meta")
-        self.L = torch.empty((k, k), device="meta")
-        self.enc = torch.empty((k // 16, n // 16, 256), dtype=torch.int16, device="meta")
-        self.buffer_rows = buffer_rows
-        self.tf32 = False
-        self.key = key
-        self.labels = torch.empty(65536, dtype=torch.int16, device="meta")
+def _member(k, n, ctx=128, rate=3, buffer_rows=128):
+    """A chain member without device state: meta tensors and a dummy label table per K."""
+    m = object.__new__(be._ChainMember)
+    m.k, m.n = k, n
+    m.W = torch.empty((k, n), device="meta")
+    m.P = torch.empty((k, n), device="meta")
+    m.E = torch.empty((k, n), device="meta")
+    m.wq = torch.empty((k, n), device="meta")
+    m.L = torch.empty((k, k), device="meta")
+    m.enc = torch.empty((k // 16, n // 16, 256), dtype=torch.int16, device="meta")
+    m.buffer_rows = buffer_rows
+    m.tf32 = False
+    m.rate = rate
+    m.ctx = ctx
+    bits = {rate} if isinstance(rate, int) else set(rate[1])
+    m.labels = {K: torch.empty(65536, dtype=torch.int16, device="meta") for K in bits}
+    return m
 
 
 def _run(monkeypatch, members, sms=148):
     launches = []
 
-    def fake_step(items, K, labels, ctx, device, max_ctas=0):
-        launches.append([(it.size_k, it.size_n, it.r0, it.end, it.tile_col0, it.n_tiles, K, ctx) for it in items])
+    def fake_step(items, ctx, device, max_ctas=0):
+        launches.append([(it.size_k, it.size_n, it.r0, it.end, it.tile_col0, it.n_tiles, it.K, ctx) for it in items])
 
     class _Props:
         multi_processor_count = sms
@@ -54,16 +58,15 @@ def _run(monkeypatch, members, sms=148):
 
 
 def test_triplet_schedule_is_valid_and_packed(monkeypatch):
-    key = (3, 1, 128)
-    gate_up = _Member(7168, 4096, key)
-    down = _Member(2048, 7168, key)
+    gate_up = _member(7168, 4096)
+    down = _member(2048, 7168)
     launches, trims = _run(monkeypatch, [gate_up, down])
     cap = 2 * 148
     seen = {}
     for items in launches:
         assert 1 <= len(items) <= _native.KQ_CHAIN_MAX_ITEMS
         assert sum(i[5] for i in items) <= cap
-        assert len({(i[6], i[7]) for i in items}) == 1
+        assert len({i[7] for i in items}) == 1
         cols = [(i[0], i[1], i[4]) for i in items]
         assert len(cols) == len(set(cols))                      # one step per chain per launch
         for k, n, r0, end, c0, nt, _, _ in items:
@@ -80,12 +83,35 @@ def test_triplet_schedule_is_valid_and_packed(monkeypatch):
     assert len(trims) == (4096 // 512) * (7168 // 128 - 1) + (7168 // 512) * (2048 // 128 - 1)
 
 
-def test_keys_never_share_a_launch_and_narrow_tail_chains(monkeypatch):
-    a = _Member(256, 16 * 40, (2, 1, 128))          # 40 tile columns: chains of 32 + 8
-    b = _Member(512, 16 * 32, (4, 1, 64))
+def test_contexts_never_share_a_launch_and_narrow_tail_chains(monkeypatch):
+    a = _member(256, 16 * 40, ctx=128, rate=2)       # 40 tile columns: chains of 32 + 8
+    b = _member(512, 16 * 32, ctx=64, rate=4)
     launches, _ = _run(monkeypatch, [a, b], sms=16)
     widths = {i[5] for items in launches for i in items if i[1] == 16 * 40}
     assert widths == {32, 8}
     for items in launches:
-        assert len({(i[6], i[7]) for i in items}) == 1
+        assert len({i[7] for i in items}) == 1
         assert sum(i[5] for i in items) <= 2 * 16 or len(items) == 1
+
+
+def test_mixed_rate_chains(monkeypatch):
+    """n-axis rate maps split chains at K changes; k-axis maps change an item's K per step; one launch may mix
+    K (one wave), and every item's K is the map's K at its rows and columns."""
+    n_bits = ("n", tuple([2] * 8 + [4] * 8 + [3] * 16))     # 32 tile columns: runs 8 (K2), 8 (K4), 16 (K3)
+    k_bits = ("k", tuple([3] * 8 + [2] * 4 + [4] * 4))      # 16 tile rows
+    a = _member(256, 512, rate=n_bits)
+    b = _member(256, 256, rate=k_bits)
+    launches, _ = _run(monkeypatch, [a, b], sms=148)
+    assert any(len({i[6] for i in items}) > 1 for items in launches)
+    for items in launches:
+        assert sum(i[5] for i in items) <= 296
+        start = 0
+        for size_k, size_n, r0, end, c0, nt, K, ctx in items:
+            assert start % 2 == 0
+            start += nt
+            if size_n == 512:
+                assert len(set(n_bits[1][c0:c0 + nt])) == 1 and K == n_bits[1][c0]
+            else:
+                assert K == k_bits[1][r0 // 16]
+    cols = sorted({(i[4], i[5]) for items in launches for i in items if i[1] == 512})
+    assert cols == [(0, 8), (8, 8), (16, 16)]
