@@ -626,6 +626,16 @@ def _buffer_rows(quant_args: dict, size_k: int) -> int:
     return rows
 
 
+def _engine_ldlq(W, Ls, quant_args, rate=None):
+    """W [B, k, n] (contiguous) and Ls [B, k, k] on the chain engine; returns (What, enc)."""
+    B, size_k, size_n = W.shape
+    wq = torch.empty_like(W)
+    enc = torch.empty((B, size_k // 16, size_n // 16, 256), dtype=torch.int16, device=W.device)
+    members = [_ChainMember(W[b], Ls[b], wq[b], enc[b], quant_args, rate=rate) for b in range(B)]
+    _chain_traverse(members, W.device)
+    return wq, enc
+
+
 def ldlq(weight: torch.Tensor, L: torch.Tensor, quant_args: dict, pb=None):
     """Block LDLQ of one matrix at uniform K (kquant/exl3_encoder_backend.py:389-505).
 
@@ -640,9 +650,12 @@ def ldlq(weight: torch.Tensor, L: torch.Tensor, quant_args: dict, pb=None):
     rows = _buffer_rows(quant_args, size_k)
     with torch.cuda.stream(get_quant_stream(devices[0])):
         w = weight.to(L.device)
-        plan = _RatePlan(int(quant_args["K"]), None, 1, size_n // 16, L.device)
-        wq, enc, _ = _ldlq_traverse(w.unsqueeze(0), L.unsqueeze(0), quant_args, plan, buffer_rows=rows,
-                                    tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
+        if len(devices) == 1 and pb is None:
+            wq, enc = _engine_ldlq(w.contiguous().unsqueeze(0), L.unsqueeze(0), quant_args)
+        else:
+            plan = _RatePlan(int(quant_args["K"]), None, 1, size_n // 16, L.device)
+            wq, enc, _ = _ldlq_traverse(w.unsqueeze(0), L.unsqueeze(0), quant_args, plan, buffer_rows=rows,
+                                        tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
     _sync(devices)
     return wq[0].to(weight.device), enc[0].to(weight.device)
 
@@ -660,9 +673,12 @@ def ldlq_mixed(weight: torch.Tensor, L: torch.Tensor, quant_args: dict, pb=None)
         raise ValueError("mixed-rate LDLQ buffer must tile the EXL K dimension")
     with torch.cuda.stream(get_quant_stream(devices[0])):
         w = weight.to(L.device)
-        plan = _RatePlan([bits], axis, 1, size_n // 16, L.device)
-        wq, enc, _ = _ldlq_traverse(w.unsqueeze(0), L.unsqueeze(0), quant_args, plan, buffer_rows=rows,
-                                    tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
+        if len(devices) == 1 and pb is None:
+            wq, enc = _engine_ldlq(w.contiguous().unsqueeze(0), L.unsqueeze(0), quant_args, rate=(axis, bits))
+        else:
+            plan = _RatePlan([bits], axis, 1, size_n // 16, L.device)
+            wq, enc, _ = _ldlq_traverse(w.unsqueeze(0), L.unsqueeze(0), quant_args, plan, buffer_rows=rows,
+                                        tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
     _sync(devices)
     return wq[0].to(weight.device), enc[0].to(weight.device)
 
@@ -677,9 +693,12 @@ def ldlq_batched(weights: torch.Tensor, Ls: torch.Tensor, quant_args: dict, pb=N
     assert size_k % 16 == 0 and size_n % 128 == 0
     rows = _buffer_rows(quant_args, size_k)
     with torch.cuda.stream(get_quant_stream(devices[0])):
-        plan = _RatePlan(int(quant_args["K"]), None, B, size_n // 16, weights.device)
-        wq, enc, _ = _ldlq_traverse(weights, Ls, quant_args, plan, buffer_rows=rows,
-                                    tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
+        if len(devices) == 1 and pb is None:
+            wq, enc = _engine_ldlq(weights.contiguous(), Ls, quant_args)
+        else:
+            plan = _RatePlan(int(quant_args["K"]), None, B, size_n // 16, weights.device)
+            wq, enc, _ = _ldlq_traverse(weights, Ls, quant_args, plan, buffer_rows=rows,
+                                        tf32=bool(quant_args.get("ldlq_tf32", False)), pb=pb)
     _sync(devices)
     return wq, enc
 
