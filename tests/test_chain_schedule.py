@@ -115,3 +115,55 @@ def test_mixed_rate_chains(monkeypatch):
                 assert K == k_bits[1][r0 // 16]
     cols = sorted({(i[4], i[5]) for items in launches for i in items if i[1] == 512})
     assert cols == [(0, 8), (8, 8), (16, 16)]
+
+
+def test_k_axis_prefix_trie_forks(monkeypatch):
+    """The k-axis candidate trie on the chain engine (host logic only): every candidate ends in one leaf, every
+    step a member runs uses a K that all of the member's candidates map to at those rows, and every chain
+    lineage covers all k/16 steps."""
+    import contextlib
+
+    k, n = 512, 256
+    runs = []
+
+    def fake_item(self):
+        r0, _ = self.steps[self.pos]
+        runs.append((id(self.m), self.tile_col0, r0, self.K))
+        return None
+
+    class _Props:
+        multi_processor_count = 148
+
+    monkeypatch.setattr(be._Chain, "item", fake_item)
+    monkeypatch.setattr(_native, "ldlq_chain_step", lambda items, ctx, device, max_ctas=0: None)
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda device: _Props())
+    monkeypatch.setattr(torch.cuda, "stream", lambda s: contextlib.nullcontext())
+    monkeypatch.setattr(be, "get_quant_stream", lambda d: None)
+    monkeypatch.setattr(be, "_sync", lambda devices: None)
+    monkeypatch.setattr(be, "_labels_for", lambda device, bits, kind, lut: torch.empty(65536, device="meta"))
+    nt = k // 16
+    maps = [tuple([3] * nt),
+            tuple([2] * 8 + [4] * 8 + [3] * 16),          # differs in the top two buffers
+            tuple([4] * 8 + [2] * 8 + [3] * 16),
+            tuple([3] * 8 + [2] * 4 + [4] * 4 + [3] * 16)]  # differs only in the second buffer
+    args = [{"K": 3, "devices": ["meta"], "mixed_rate_axis": "k", "mixed_tile_bits": m, "tailbite_context": 128}
+            for m in maps]
+    W = torch.empty((2, k, n), device="meta")
+    Ls = torch.empty((2, k, k), device="meta")
+    wq, enc = be.ldlq_mixed_k_candidates_prefix_reuse(W, Ls, [args, args[:2]])
+    assert wq.shape == (6, k, n) and enc.shape == (6, k // 16, n // 16, 256)
+    by_member = {}
+    for mid, c0, r0, K in runs:
+        by_member.setdefault(mid, []).append((c0, r0, K))
+    # members that ran steps: each step's K is one of the candidate maps' K at that row
+    for steps in by_member.values():
+        for c0, r0, K in steps:
+            assert K in {m[r0 // 16] for m in maps}
+    # each chain column range: the rows run by its lineage cover all k/16 steps at least once per leaf path
+    rows_per_col = {}
+    for mid, c0, r0, K in runs:
+        rows_per_col.setdefault(c0, set()).add(r0)
+    assert all(rows == set(range(0, k, 16)) for rows in rows_per_col.values())
+    # the shared bottom buffers ran once per source (no forks below the top two buffers)
+    bottom = [r for r in runs if r[2] >= 256]
+    assert len(bottom) == 2 * (n // 16 // 32 or 1) * (256 // 16)
