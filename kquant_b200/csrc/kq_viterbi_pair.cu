@@ -362,17 +362,10 @@ __host__ __device__ constexpr size_t pair_smem_bytes() {
            kJobs * 2 * 4;
 }
 
-// The kernel body for one K; dec_base is this CTA's decision area
-// (kJobs x 256 rows of PairMap<K>::ROW_BYTES).  The single-K kernels hold the
-// body inline; the mixed-K chain kernel calls this device copy per CTA.
-template <int K, class IO>
-__device__ __forceinline__ void pair_body(const IO& io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
-                                          const __half* __restrict__ labels16, int C, int njobs,
-                                          uint8_t* __restrict__ dec_base)
-{
-#include "kq_viterbi_pair_body.inc"
-}
-
+// The kernel body (kq_viterbi_pair_body.inc) is included inline in each
+// kernel, with K, IO and the parameters in scope: the single-K kernels below
+// and, once per K, the mixed-K chain kernel.  (A shared __device__ function
+// taking the parameters by reference made every variant about 4% slower.)
 template <int K, class IO>
 __global__ void __launch_bounds__(kThreads, 1)
 pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
@@ -390,20 +383,27 @@ constexpr size_t kMaxRowBytes =
 
 // Chain launch whose items may differ in K: one tile pair per CTA (a single
 // wave), each CTA running the body for its pair's K with that item's labels.
+// (A template on IO so that the body's `if constexpr` branches are discarded.)
+template <class IO>
 __global__ void __launch_bounds__(kThreads, 1)
-pair_kernel_mk(const __grid_constant__ ChainIO io, int64_t n_tiles, int C, uint8_t* __restrict__ decisions)
+pair_kernel_mk(const IO io, int64_t n_tiles, int C, uint8_t* __restrict__ decisions)
 {
-    const kq_chain_item& c = io.it[io.find(2 * (int64_t)blockIdx.x)];
-    uint8_t* dec = decisions + (size_t)blockIdx.x * kJobs * 256 * kMaxRowBytes;
-    const uint32_t* l32 = reinterpret_cast<const uint32_t*>(c.labels);
-    const __half* l16 = reinterpret_cast<const __half*>(c.labels);
-    switch (c.K) {
-    case 2: pair_body<2, ChainIO>(io, n_tiles, l32, l16, C, 1, dec); break;
-    case 3: pair_body<3, ChainIO>(io, n_tiles, l32, l16, C, 1, dec); break;
-    default: pair_body<4, ChainIO>(io, n_tiles, l32, l16, C, 1, dec); break;
+    const kq_chain_item& item = io.it[io.find(2 * (int64_t)blockIdx.x)];
+    uint8_t* dec_base = decisions + (size_t)blockIdx.x * kJobs * 256 * kMaxRowBytes;
+    const uint32_t* __restrict__ labels32 = reinterpret_cast<const uint32_t*>(item.labels);
+    const __half* __restrict__ labels16 = reinterpret_cast<const __half*>(item.labels);
+    const int njobs = 1;
+    if (item.K == 2) {
+        constexpr int K = 2;
+#include "kq_viterbi_pair_body.inc"
+    } else if (item.K == 3) {
+        constexpr int K = 3;
+#include "kq_viterbi_pair_body.inc"
+    } else {
+        constexpr int K = 4;
+#include "kq_viterbi_pair_body.inc"
     }
 }
-
 
 template <int K>
 void pair_grid(int64_t n, int sms, int& grid, int& njobs) {
@@ -607,8 +607,8 @@ extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int t
     if (kmask & 8) sm = std::max(sm, pair_smem_bytes<3>());
     if (kmask & 16) sm = std::max(sm, pair_smem_bytes<4>());
     sm = ((sm + 15) & ~(size_t)15) + (size_t)ChainIO::kStageFloats * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(pair_kernel_mk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    cudaError_t e = cudaFuncSetAttribute(pair_kernel_mk<ChainIO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
-    pair_kernel_mk<<<(int)pairs, kThreads, sm, s>>>(io, total, tailbite_ctx, static_cast<uint8_t*>(workspace));
+    pair_kernel_mk<ChainIO><<<(int)pairs, kThreads, sm, s>>>(io, total, tailbite_ctx, static_cast<uint8_t*>(workspace));
     return check_launch("pair_kernel_mk");
 }
