@@ -275,3 +275,25 @@ def test_candidate_reuse_equals_independent_encodes(cuda_device, axis):
             assert torch.equal(enc_r[f], enc_o[0]), (s, c)
             assert torch.equal(wq_r[f], wq_o[0]), (s, c)
             f += 1
+
+
+@pytest.mark.parametrize("axis", ["n", "k"])
+def test_qsrt_batch_candidates_equal_single_encodes(cuda_device, axis):
+    """kquant's production call (quantize_qsrt_batch, reuse engines) == quantize_qsrt per candidate, which the
+    reference fixtures pin: scales and codes bit for bit, proxies to float rounding."""
+    dev = cuda_device
+    k, n = (256, 512) if axis == "n" else (512, 256)
+    w, h = _problem(dev, k=k, n=n, seed=90)
+    nt = (n if axis == "n" else k) // 16
+    maps = [tuple([3] * nt), tuple([2] * 8 + [4] * 8 + [3] * (nt - 16)),
+            tuple([2] * 8 + [4] * 8 + [2] * 8 + [4] * 8 + [3] * (nt - 32))]
+    group = [_args(dev, mixed_rate_axis=axis, mixed_tile_bits=m) for m in maps]
+    batch = be.quantize_qsrt_batch([w.clone()], [make_shared_h(k, dev, h)], [group])[0]
+    for m, cand in zip(maps, batch):
+        # pack_trellis_fn (kquant/exl3_encoder_backend.py quantize_qsrt) returning the raw states
+        _, proxy, out = be.quantize_qsrt(w.clone(), make_shared_h(k, dev, h),
+                                         _args(dev, mixed_rate_axis=axis, mixed_tile_bits=m,
+                                               pack_trellis_fn=lambda enc, qa: enc.clone()), False)
+        assert torch.equal(out["suh"], cand["suh"]) and torch.equal(out["svh"], cand["svh"])
+        assert torch.equal(out["trellis"], cand["encoded"])
+        assert abs(proxy - cand["proxy"]) <= 1e-6 * max(proxy, 1e-12)
