@@ -1956,8 +1956,10 @@ def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None
                 sel.append(c)
                 tot += c.n_tiles
         if len({c.K for c in sel}) > 1:
-            # different K share a launch only as one wave with pair-aligned items
-            sel.sort(key=lambda c: c.n_tiles % 2)
+            # Items of different K share a launch only pair-aligned: odd-length
+            # chains (an odd run of one K along n) go last, at most one of them.
+            odd = [c for c in sel if c.n_tiles % 2]
+            sel = [c for c in sel if not c.n_tiles % 2] + odd[:1]
         _native.ldlq_chain_step([c.item() for c in sel], ctx, device)
         for c in sel:
             c.advance()

@@ -167,3 +167,22 @@ def test_k_axis_prefix_trie_forks(monkeypatch):
     # the shared bottom buffers ran once per source (no forks below the top two buffers)
     bottom = [r for r in runs if r[2] >= 256]
     assert len(bottom) == 2 * (n // 16 // 32 or 1) * (256 // 16)
+
+
+def test_odd_runs_stay_pair_aligned(monkeypatch):
+    """Odd-length K runs along n (single tile columns) never leave two odd items in a mixed-K launch."""
+    bits = ("n", tuple([2, 3, 4, 3, 2, 4, 4, 4] * 4))        # runs of length 1 and 3
+    a = _member(256, 512, rate=bits)
+    launches, _ = _run(monkeypatch, [a], sms=148)
+    for items in launches:
+        if len({i[6] for i in items}) > 1:
+            starts, at = [], 0
+            for i in items:
+                starts.append(at)
+                at += i[5]
+            assert all(x % 2 == 0 for x in starts)
+    cols = {}
+    for items in launches:
+        for i in items:
+            cols.setdefault((i[4], i[5]), []).append(i[2])
+    assert all(len(r) == 256 // 16 for r in cols.values())
