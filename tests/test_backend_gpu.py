@@ -297,3 +297,16 @@ def test_qsrt_batch_candidates_equal_single_encodes(cuda_device, axis):
         assert torch.equal(out["suh"], cand["suh"]) and torch.equal(out["svh"], cand["svh"])
         assert torch.equal(out["trellis"], cand["encoded"])
         assert abs(proxy - cand["proxy"]) <= 1e-6 * max(proxy, 1e-12)
+
+
+def test_mixed_chain_engine_odd_runs(cuda_device):
+    """n-axis maps with single-column K runs (odd-length chains in mixed-K launches) == the unfused path."""
+    dev = cuda_device
+    W, Ls, nt = _mixed_case(dev, "n", 80)
+    maps = [tuple((2, 3, 4, 3, 2, 4, 4, 4)[i % 8] for i in range(nt)),
+            tuple((3, 2, 2, 4, 3, 3, 4, 2)[i % 8] for i in range(nt))]
+    qal = [_args(dev, mixed_rate_axis="n", mixed_tile_bits=m) for m in maps]
+    wq_c, enc_c = be.ldlq_mixed_batched(W, Ls, qal)
+    wq_o, enc_o = _old_path(W, Ls, qal)
+    assert torch.equal(enc_c, enc_o)
+    assert torch.equal(wq_c, wq_o)
