@@ -3,6 +3,11 @@
 //     trace:  out += sum_{i < M, j < N} (A B^T)[i][j] * D[i][j]
 //     store:  D = alpha * A B^T + beta * D
 //
+// and the calibration-Hessian accumulation built on the store GEMM
+// (kq_accumulate_hessian, kquant/capture.py:713-730): an operand kernel
+// (transpose, weighting, TF32 hi/lo split) and one symmetric 3xTF32 launch
+// over the upper-triangle tiles (abt_seg_kernel<SYM, X3>, described below).
+//
 // A [M x Kd] and B [N x Kd] are row-major fp32 (both K-major); D [M x N]
 // has row stride ldd.  The proxy error numerator of the encoder,
 // tr(E^T H E) (kquant/exl3_encoder_backend.py:1466-1492), is this with

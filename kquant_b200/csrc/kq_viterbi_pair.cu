@@ -21,6 +21,11 @@
 //    one another, and a job's traceback phase (C or 256 steps) never
 //    outlasts the other job's forward phase (2C or 256 steps), so the stagger
 //    keeps the ALU busy without a second buffer.
+//  * Tile I/O is a policy: FlatIO (tiles in trellis order), StepIO (one LDLQ
+//    step: gather W + comp, scatter What / E / states) and ChainIO (LDLQ
+//    chain items at their own rows, the feedback product computed in the
+//    load).  pair_kernel_mk runs a single-wave chain launch whose items
+//    differ in K, each CTA on its pair's K.
 #include <algorithm>
 #include "kq_viterbi_common.cuh"
 
