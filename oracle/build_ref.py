@@ -25,7 +25,15 @@ HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 MODULE = "kquant_ref_sqg"
 OUT = OUT_DIR / f"{MODULE}.so"
-DEFAULT_REF = Path("/root/reference")
+
+
+def default_root() -> Path:
+    """The reference checkout: $KQ_REFERENCE_ROOT, else a ``reference`` directory beside this repository."""
+    env = os.environ.get("KQ_REFERENCE_ROOT")
+    return Path(env) if env else HERE.parents[1] / "reference"
+
+
+DEFAULT_REF = default_root()
 
 
 def available(ref_root: Path = DEFAULT_REF) -> bool:

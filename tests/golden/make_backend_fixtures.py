@@ -84,7 +84,9 @@ def _load_reference_backend(ref_root: Path):
 
 
 def main():
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: make_backend_fixtures.py REFERENCE_ROOT [case ...]")
+    ref_root = Path(sys.argv[1])
     be = _load_reference_backend(ref_root)
     only = set(sys.argv[2:])
     for name, case in CASES.items():

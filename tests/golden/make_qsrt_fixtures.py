@@ -15,7 +15,9 @@ from tests.golden.qsrt_cases import CASES, SHAPES, legal_states, scales  # noqa:
 
 
 def main():
-    sys.path.insert(0, sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: make_qsrt_fixtures.py REFERENCE_ROOT")
+    sys.path.insert(0, sys.argv[1])
     from kquant import qsrt
     out = {}
     for mode, axis in CASES:

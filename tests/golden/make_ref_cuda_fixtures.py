@@ -1,0 +1,181 @@
+"""Record fixtures from the REFERENCE backend running on a CUDA GPU (test infrastructure).
+
+The reference's ``kquant/exl3_encoder_backend.py`` is loaded with its own loader
+(``kquant.exl3_loader.load_qsrt_encoder``) and its own SQG quantizer hook
+(``kquant.sqg_quantizer.install_sqg_quantizer``).  The hook's CUDA extension is
+the reference's kernel compiled from its sources into ``oracle/_ref`` (the
+reference's JIT loader is replaced by that prebuilt module).  Only the
+un-vendored ExLlamaV3 helpers are stubbed, as the decoder contract defines
+them: a Sylvester Hadamard normalised 1/sqrt(n) (kquant/exl3_reference.py:195-212)
+and ``pack_trellis`` = ``kquant.qsrt.pack_trellis_edges``.
+
+For every case of ``tests/golden/ref_cuda_cases.py`` the script records, as
+digests and scalars:
+
+* ``ref``: the reference's own end-to-end result (its rotated W and L at the
+  LDLQ call, fp16 scales, g_scale, states, proxy, a sample of the
+  reconstruction);
+* ``kq_prep``: the digests of this backend's rotated W and L for the same
+  inputs (so a test can prove it feeds identical inputs);
+* ``ref_on_kq_prep``: the reference's LDLQ run on exactly this backend's
+  rotated W and L (codes that this backend must reproduce bit for bit).
+
+Usage (on a GPU host, the reference package importable from KQ_REFERENCE_ROOT):
+    KQ_REFERENCE_ROOT=baseline/_ref python tests/golden/make_ref_cuda_fixtures.py OUT.json [case ...]
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+import tempfile
+import types
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+from tests.golden import ref_cuda_cases as C  # noqa: E402
+
+
+def load_reference_backend(ref_root: Path):
+    sys.path.insert(0, str(ref_root))
+    from kquant import qsrt, sqg_quantizer
+    from kquant.exl3_loader import load_qsrt_encoder
+    from oracle import build_ref
+
+    def had(n, device, dtype, scale):
+        h = torch.ones((1, 1), dtype=torch.float64)
+        while h.shape[0] < n:
+            h = torch.cat((torch.cat((h, h), 1), torch.cat((h, -h), 1)), 0)
+        return (h * scale).to(device=device, dtype=dtype)
+
+    stubs = {
+        "exllamav3.ext": types.SimpleNamespace(exllamav3_ext=types.SimpleNamespace()),
+        "exllamav3.util.hadamard": types.SimpleNamespace(get_hadamard_dt=had),
+        "exllamav3.util.tensor": types.SimpleNamespace(save_tensor_image=lambda *a, **k: None),
+    }
+    for name, mod in stubs.items():
+        m = types.ModuleType(name)
+        m.__dict__.update(vars(mod))
+        sys.modules[name] = m
+    module = load_qsrt_encoder(Path(tempfile.mkdtemp()))
+    ext = build_ref.load()
+    sqg_quantizer._extension = lambda: ext
+    sqg_quantizer.install_sqg_quantizer(module)
+    module.pack_trellis = lambda enc, qa: qsrt.pack_trellis_edges(enc, qa["K"])
+    return module
+
+
+def _states(module_qsrt, trellis, K):
+    return module_qsrt.unpack_trellis_states(trellis.cpu(), K).to(torch.int16)
+
+
+def run_qsrt_case(name, ref, kq, device):
+    from kquant import qsrt as ref_qsrt
+    from kquant.ldlq import make_shared_h as ref_shared
+    from kquant_b200.ldlq import make_shared_h as kq_shared
+    out = {}
+    # reference end to end
+    w, h, args = C.qsrt_inputs(name, device)
+    with C.Capture(ref) as cap:
+        wq, proxy, tens = ref.quantize_qsrt(w.clone(), ref_shared(w.shape[0], device, h), args, True)
+    torch.cuda.synchronize()
+    states = _states(ref_qsrt, tens["trellis"], args["K"])
+    idx = C.sample_index(wq.numel())
+    out["ref"] = {"w_r": C.digest(cap.inputs[0]), "L": C.digest(cap.inputs[1]), "suh": C.digest(tens["suh"]),
+                  "svh": C.digest(tens["svh"]), "g_scale": float(args["g_scale"]), "proxy": float(proxy),
+                  "states": C.digest(states), "state_rows": C.row_digests(states),
+                  "trellis": C.digest(tens["trellis"]), "weight_q": C.digest(wq),
+                  "weight_q_sample": wq.flatten()[idx.to(device)].cpu().tolist()}
+    ref_inputs = cap.inputs
+    # this backend's preparation on the same inputs
+    w, h, args = C.qsrt_inputs(name, device)
+    with C.Capture(kq) as kcap:
+        kwq, kproxy, ktens = kq.quantize_qsrt(w.clone(), kq_shared(w.shape[0], device, h), args, True)
+    torch.cuda.synchronize()
+    kstates = _states(ref_qsrt, ktens["trellis"], args["K"])
+    out["kq_prep"] = {"w_r": C.digest(kcap.inputs[0]), "L": C.digest(kcap.inputs[1]),
+                      "suh": C.digest(ktens["suh"]), "svh": C.digest(ktens["svh"]),
+                      "g_scale": float(args["g_scale"])}
+    out["prep_equal"] = {key: out["ref"][key] == out["kq_prep"][key] for key in ("w_r", "L", "suh", "svh")}
+    # the reference's LDLQ on this backend's rotated inputs
+    _, _, args = C.qsrt_inputs(name, device)
+    rwq, renc = ref.ldlq(kcap.inputs[0].clone(), kcap.inputs[1].clone(), args)
+    torch.cuda.synchronize()
+    renc = renc.to(torch.int16)
+    out["ref_on_kq_prep"] = {"states": C.digest(renc), "state_rows": C.row_digests(renc),
+                             "weight_q": C.digest(rwq)}
+    # informational: how this run of this backend compared (the test repeats it)
+    out["kq_check"] = {"states_equal_ref_on_kq_prep": C.digest(kstates) == out["ref_on_kq_prep"]["states"],
+                       "proxy": float(kproxy),
+                       "proxy_rel": abs(float(kproxy) - float(proxy)) / float(proxy)}
+    del ref_inputs
+    return out
+
+
+def run_batch_case(name, ref, kq, device):
+    from kquant.ldlq import make_shared_h as ref_shared
+    ws, hs, groups = C.batch_inputs(name, device)
+    res = ref.quantize_qsrt_batch([w.clone() for w in ws], [ref_shared(w.shape[0], device, h)
+                                                             for w, h in zip(ws, hs)], groups)
+    torch.cuda.synchronize()
+    out = {"sources": []}
+    for s, cands in enumerate(res):
+        rows = []
+        for c in cands:
+            idx = C.sample_index(c["weight_q"].numel())
+            rows.append({"states": C.digest(c["encoded"].to(torch.int16)), "suh": C.digest(c["suh"]),
+                         "svh": C.digest(c["svh"]), "proxy": float(c["proxy"]), "g_scale": float(c["g_scale"]),
+                         "weight_q_sample": c["weight_q"].flatten()[idx.to(device)].cpu().tolist()})
+        out["sources"].append(rows)
+    return out
+
+
+def run_uniform_case(name, ref, kq, device):
+    from kquant import qsrt as ref_qsrt
+    from kquant.ldlq import make_shared_h as ref_shared
+    ws, h, args = C.uniform_inputs(name, device)
+    shared = ref_shared(ws[0].shape[0], device, h)
+    res = ref.quantize_uniform_batch([w.clone() for w in ws], [shared, shared], args)
+    torch.cuda.synchronize()
+    out = {"members": []}
+    for t, (proxy, tens) in enumerate(res):
+        states = _states(ref_qsrt, tens["trellis"], args[t]["K"])
+        out["members"].append({"states": C.digest(states), "suh": C.digest(tens["suh"]),
+                               "svh": C.digest(tens["svh"]), "proxy": float(proxy),
+                               "g_scale": float(args[t]["g_scale"])})
+    return out
+
+
+def main():
+    if len(sys.argv) < 2:
+        raise SystemExit(__doc__)
+    root = os.environ.get("KQ_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("set KQ_REFERENCE_ROOT to the directory that holds the reference's kquant package")
+    out_path = Path(sys.argv[1])
+    only = set(sys.argv[2:])
+    device = torch.device("cuda:0")
+    torch.cuda.set_device(device)
+    ref = load_reference_backend(Path(root).resolve())
+    from kquant_b200 import exl3_encoder_backend as kq
+    fixtures = {"device": torch.cuda.get_device_name(device), "torch": torch.__version__, "cases": {}}
+    runners = [(C.QSRT_CASES, run_qsrt_case), (C.BATCH_CASES, run_batch_case), (C.UNIFORM_CASES, run_uniform_case)]
+    for cases, runner in runners:
+        for name in cases:
+            if only and name not in only:
+                continue
+            fixtures["cases"][name] = runner(name, ref, kq, device)
+            print(name, json.dumps({k: v for k, v in fixtures["cases"][name].items()
+                                    if k in ("prep_equal", "kq_check")}), flush=True)
+    out_path.parent.mkdir(parents=True, exist_ok=True)
+    out_path.write_text(json.dumps(fixtures, indent=1))
+    print("wrote", out_path)
+
+
+if __name__ == "__main__":
+    main()
