@@ -149,12 +149,15 @@ typedef struct {
  * share the launch.  Replaces the per-step feedback + quantize of
  * kquant/exl3_encoder_backend.py:389-505 (ldlq) / :1495-1583 (ldlq_batched);
  * the buffer-end update P[:begin] += L^T err stays with the caller.
- * Items carry their own K and label table.  When they all share K the
- * launch may hold any number of tiles; items of different K share one
- * launch only if it is a single wave (at most 2 tiles per SM) and every item
- * starts at an even tile, so that each CTA's tile pair has one K.  Workspace
- * as kq_viterbi_encode (K = 3) for the total tile count; max_ctas as
- * kq_ldlq_step_encode (uniform-K launches only).
+ * Items carry their own K and label table.  When they all share both the
+ * launch may hold any number of tiles.  Items of different K (or label
+ * tables) share a launch when every item starts at an even tile (so each
+ * tile pair has one K) and either the launch has at most one pair per SM
+ * (one pair per CTA) or the pairs of each (K, labels) group, two to a CTA,
+ * need at most one CTA per SM; a CTA with two pairs hides each pair's
+ * tracebacks under the other's forward steps.  Workspace as
+ * kq_viterbi_encode (K = 3) for the total tile count; max_ctas as
+ * kq_ldlq_step_encode.
  */
 int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int tailbite_ctx, int max_ctas, void* workspace,
                        size_t workspace_bytes, void* stream);
@@ -186,9 +189,13 @@ int kq_unpack_trellis_states(const uint16_t* packed, int64_t n_tiles, int K, uin
  * results as kq_quantize_tiles_sqg, but no workspace argument: its scratch
  * (label table + decision rows, 32 MiB + 128 KiB) is a fixed __device__
  * array that every GPU loading this library holds until exit.  At most
- * KQ_NOALLOC_MAX_TILES tiles per call; larger counts return KQ_ERR_ARG.
- * The first call on a device resolves the scratch address for that device;
- * make that call before any stream capture.  All calls share one scratch:
+ * KQ_NOALLOC_MAX_TILES tiles per call, a chosen bound on one call's latency
+ * (not a limit of the scratch); larger counts return KQ_ERR_ARG.  The fixed
+ * decision rows cap the grid at 8 CTAs (K2, K3) or 16 CTAs (K4), so a call
+ * runs about 18x (K2, K3) or 9x (K4) slower than kq_quantize_tiles_sqg.
+ * The first call on a device resolves the scratch address for that device
+ * and caches it for the process: make that call before any stream capture,
+ * and do not reset the device afterwards.  All calls share one scratch:
  * calls that overlap on the GPU (different streams, or different host
  * threads) race and corrupt each other's results; serialize them.
  */

@@ -16,7 +16,7 @@ constexpr size_t kLabelBytes = 65536 * 2;
 
 int quantize_with_kind(const float* tiles, float* vals, uint16_t* states, int64_t n, int kind, const uint8_t* lut,
                        int K, int C, void* ws, size_t ws_bytes, void* stream) {
-    if (K < 2 || K > 4) { kq::set_error("quantize_tiles: K must be 2, 3 or 4 (got %d)", K); return KQ_ERR_ARG; }
+    if (K < 1 || K > 8) { kq::set_error("quantize_tiles: K must be in 1..8 (got %d)", K); return KQ_ERR_ARG; }
     if (C < 1 || C > 128) { kq::set_error("tailbite_context must be in 1..128 (got %d)", C); return KQ_ERR_ARG; }
     if (n < 0) { kq::set_error("quantize_tiles: negative tile count"); return KQ_ERR_ARG; }
     if (n == 0) return KQ_OK;
@@ -40,7 +40,7 @@ int kq_build_labels(int kind, const uint8_t* lut, uint16_t* labels, void* stream
 }
 
 size_t kq_viterbi_workspace_bytes(int K, int64_t n_tiles) {
-    if (K < 2 || K > 4 || n_tiles < 0) return 0;
+    if (K < 1 || K > 8 || n_tiles < 0) return 0;
     return kLabelBytes + kq::viterbi_decision_bytes(K, n_tiles);
 }
 

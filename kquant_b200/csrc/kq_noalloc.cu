@@ -9,6 +9,18 @@
 // file-scope __device__ array of fixed size, which every GPU that loads this
 // library holds until process exit.  The caller still passes its own input
 // and output buffers.
+//
+// The decision rows bound the grid: 32 MiB / (2 jobs x 256 rows x row bytes)
+// is 8 CTAs at K2 and K3 (8 KiB rows) and 16 at K4 (4 KiB rows), against 148
+// SMs.  Each CTA loops over its tile pairs, so results are exact, but a call
+// runs about 9x (K4) to 18x (K2, K3) slower than kq_quantize_tiles_sqg with a
+// full workspace.  The 4,096-tile cap is a chosen per-call bound (it keeps one
+// call to a few tens of milliseconds); the scratch itself would serve any count.
+//
+// The scratch address is resolved once per device index and cached for the
+// life of the process: the entry point assumes one primary context per device
+// that is never reset (cudaDeviceReset or a context teardown would leave the
+// cached address stale).
 #include <mutex>
 #include "kq_common.cuh"
 
@@ -58,7 +70,7 @@ extern "C" int kq_quantize_tiles_sqg_noalloc(const float* tiles, float* out_vals
                                              int64_t n_tiles, const uint8_t* lut, int K, int tailbite_ctx,
                                              void* stream) {
     if (n_tiles < 0 || n_tiles > KQ_NOALLOC_MAX_TILES) {
-        kq::set_error("kq_quantize_tiles_sqg_noalloc: n_tiles=%lld outside 0..%d (fixed scratch limit)",
+        kq::set_error("kq_quantize_tiles_sqg_noalloc: n_tiles=%lld outside 0..%d (the per-call bound)",
                       (long long)n_tiles, KQ_NOALLOC_MAX_TILES);
         return KQ_ERR_ARG;
     }

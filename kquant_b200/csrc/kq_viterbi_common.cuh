@@ -32,4 +32,29 @@ __device__ __forceinline__ int key_node(uint32_t key) {
     else return (((slot & 15) << 5) | lane) + ((slot >> 4) << 9) + (j << 10);
 }
 
+// Tie key for any K in 1..8 (the wide kernel): K2 as above; every other K
+// takes the reference's 512-thread two-stream scan (e = thread + 512 s +
+// 1024 j, j up to 31 at K1), so j gets five bits.
+template <int K>
+__device__ __forceinline__ uint32_t wide_tie_key(int e) {
+    if constexpr (K == 2) {
+        return tie_key<2>(e);
+    } else {
+        const int t = e & 511, s = (e >> 9) & 1, j = e >> 10;
+        return (brev5(16 * s + (t >> 5)) << 10) | (brev5(t & 31) << 5) | j;
+    }
+}
+
+template <int K>
+__device__ __forceinline__ int wide_key_node(uint32_t key) {
+    if constexpr (K == 2) {
+        return key_node<2>(key);
+    } else {
+        const int j = key & 31;
+        const int lane = brev5((key >> 5) & 31);
+        const int slot = brev5((key >> 10) & 31);
+        return (((slot & 15) << 5) | lane) + ((slot >> 4) << 9) + (j << 10);
+    }
+}
+
 }  // namespace kq

@@ -35,6 +35,7 @@ namespace {
 constexpr int kThreads = 512;
 constexpr int kJobs = 2;
 constexpr int kStageBufs = 4;   // traceback row staging: buffers in the cp.async pipeline
+constexpr int kMaxChainCtas = 160;   // CTAs of a mixed-K chain launch (one per SM)
 
 template <int K>
 struct PairMap {
@@ -288,6 +289,8 @@ struct ChainIO {
     kq_chain_item it[KQ_CHAIN_MAX_ITEMS];
     int64_t start[KQ_CHAIN_MAX_ITEMS + 1];
     int n;
+    // Mixed-K launches: the tile pairs of CTA b (-1: none); both of one K.
+    int16_t cta_pair[kMaxChainCtas][kJobs];
     __device__ __forceinline__ int find(int64_t tile) const {
         int i = 0;
         while (i + 1 < n && tile >= start[i + 1]) ++i;
@@ -377,6 +380,7 @@ pair_kernel(const IO io, int64_t n_tiles, const uint32_t* __restrict__ labels32,
             const __half* __restrict__ labels16, int C, int njobs, uint8_t* __restrict__ decisions)
 {
     uint8_t* dec_base = decisions + (size_t)blockIdx.x * kJobs * 256 * PairMap<K>::ROW_BYTES;
+    auto pair_index = [&](int64_t t) { return (int64_t)blockIdx.x + (int64_t)gridDim.x * t; };
 #include "kq_viterbi_pair_body.inc"
 }
 
@@ -386,18 +390,27 @@ constexpr size_t kMaxRowBytes =
         ? (PairMap<2>::ROW_BYTES > PairMap<4>::ROW_BYTES ? PairMap<2>::ROW_BYTES : PairMap<4>::ROW_BYTES)
         : (PairMap<3>::ROW_BYTES > PairMap<4>::ROW_BYTES ? PairMap<3>::ROW_BYTES : PairMap<4>::ROW_BYTES);
 
-// Chain launch whose items may differ in K: one tile pair per CTA (a single
-// wave), each CTA running the body for its pair's K with that item's labels.
-// (A template on IO so that the body's `if constexpr` branches are discarded.)
+// Chain launch whose items may differ in K: each CTA runs one or two tile
+// pairs of one K (the host's per-CTA pair table, io.cta_pair), with the body
+// for that K and that item's labels.  Two pairs per CTA stagger like the
+// single-K kernel's jobs, hiding each pair's tracebacks under the other's
+// forward steps.  (A template on IO so that the body's `if constexpr`
+// branches are discarded.)
 template <class IO>
 __global__ void __launch_bounds__(kThreads, 1)
 pair_kernel_mk(const IO io, int64_t n_tiles, int C, uint8_t* __restrict__ decisions)
 {
-    const kq_chain_item& item = io.it[io.find(2 * (int64_t)blockIdx.x)];
+    const int64_t n_pairs_all = (n_tiles + 1) >> 1;
+    auto pair_index = [&](int64_t t) -> int64_t {
+        if (t >= kJobs) return n_pairs_all;
+        const int q = io.cta_pair[blockIdx.x][t];
+        return q < 0 ? n_pairs_all : (int64_t)q;
+    };
+    const kq_chain_item& item = io.it[io.find(2 * pair_index(0))];
     uint8_t* dec_base = decisions + (size_t)blockIdx.x * kJobs * 256 * kMaxRowBytes;
     const uint32_t* __restrict__ labels32 = reinterpret_cast<const uint32_t*>(item.labels);
     const __half* __restrict__ labels16 = reinterpret_cast<const __half*>(item.labels);
-    const int njobs = 1;
+    const int njobs = io.cta_pair[blockIdx.x][1] >= 0 ? kJobs : 1;
     if (item.K == 2) {
         constexpr int K = 2;
 #include "kq_viterbi_pair_body.inc"
@@ -582,7 +595,7 @@ extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int t
                       (long long)c.tile_col0, (long long)c.n_tiles);
             return KQ_ERR_ARG;
         }
-        mixed |= c.K != items[0].K;
+        mixed |= c.K != items[0].K || c.labels != items[0].labels;
         even &= (total % 2) == 0;
         kmask |= 1 << c.K;
         io.it[i] = c;
@@ -596,13 +609,58 @@ extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int t
                                 static_cast<uint8_t*>(workspace), workspace_bytes, s);
     int sms = 0;
     if (int rc = sm_count(&sms)) return rc;
-    const int64_t pairs = (total + 1) / 2;
-    if (pairs > sms || !even) {
-        set_error("kq_ldlq_chain_step: items of different K need one wave (%lld pairs > %d SMs) and even item starts",
-                  (long long)pairs, sms);
+    if (sms > kMaxChainCtas) sms = kMaxChainCtas;
+    if (!even) {
+        set_error("kq_ldlq_chain_step: items of different K need even item starts");
         return KQ_ERR_ARG;
     }
-    const size_t need = (size_t)pairs * kJobs * 256 * kMaxRowBytes;
+    // Per-CTA pair table.  At most one pair per SM: one pair per CTA.  More:
+    // the pairs of each (K, label table) two to a CTA (one when that group's
+    // count is odd), so every CTA runs one K and one codebook.
+    const int64_t pairs = (total + 1) / 2;
+    int ctas = 0;
+    if (pairs <= sms) {
+        for (int64_t p = 0; p < pairs; ++p) {
+            io.cta_pair[p][0] = (int16_t)p;
+            io.cta_pair[p][1] = -1;
+        }
+        ctas = (int)pairs;
+    }
+    bool grouped[KQ_CHAIN_MAX_ITEMS] = {};
+    for (int g = 0; g < n_items && pairs > sms && ctas <= sms; ++g) {
+        if (grouped[g]) continue;
+        int64_t q0 = -1;
+        for (int i = g; i < n_items && ctas <= sms; ++i) {
+            if (grouped[i] || items[i].K != items[g].K || items[i].labels != items[g].labels) continue;
+            grouped[i] = true;
+            for (int64_t p = io.start[i] / 2; p < (io.start[i + 1] + 1) / 2; ++p) {
+                if (q0 < 0) { q0 = p; continue; }
+                if (ctas < sms) {
+                    io.cta_pair[ctas][0] = (int16_t)q0;
+                    io.cta_pair[ctas][1] = (int16_t)p;
+                }
+                ++ctas;
+                q0 = -1;
+            }
+        }
+        if (q0 >= 0) {
+            if (ctas < sms) {
+                io.cta_pair[ctas][0] = (int16_t)q0;
+                io.cta_pair[ctas][1] = -1;
+            }
+            ++ctas;
+        }
+    }
+    if (ctas > sms || pairs > 0x7FFF) {
+        set_error("kq_ldlq_chain_step: items of different K need at most 2 same-K tile pairs per SM (%lld pairs)",
+                  (long long)pairs);
+        return KQ_ERR_ARG;
+    }
+    if (max_ctas > 0 && ctas > max_ctas) {
+        set_error("kq_ldlq_chain_step: a mixed-K launch needs %d CTAs (max_ctas %d)", ctas, max_ctas);
+        return KQ_ERR_ARG;
+    }
+    const size_t need = (size_t)ctas * kJobs * 256 * kMaxRowBytes;
     if (workspace_bytes < need) {
         set_error("viterbi workspace too small: %zu < %zu", workspace_bytes, need);
         return KQ_ERR_WORKSPACE;
@@ -614,6 +672,6 @@ extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int t
     sm = ((sm + 15) & ~(size_t)15) + (size_t)ChainIO::kStageFloats * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(pair_kernel_mk<ChainIO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) { set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e)); return KQ_ERR_CUDA; }
-    pair_kernel_mk<ChainIO><<<(int)pairs, kThreads, sm, s>>>(io, total, tailbite_ctx, static_cast<uint8_t*>(workspace));
+    pair_kernel_mk<ChainIO><<<ctas, kThreads, sm, s>>>(io, total, tailbite_ctx, static_cast<uint8_t*>(workspace));
     return check_launch("pair_kernel_mk");
 }

@@ -41,6 +41,11 @@ codebook_mul1_mult = 0x83DCD12D
 # --------------------------------------------------------------------------
 
 
+# Trellis rates the tile kernels cover: K2..K4 on the tile-pair kernel, K1 and
+# K5..K8 on the wide-butterfly kernel.
+TRELLIS_BITS = (1, 2, 3, 4, 5, 6, 7, 8)
+
+
 def _tc_order() -> list[int]:
     """Row-major 16x16 index visited at each trellis position (EXL tensor-core order).
 
@@ -149,8 +154,8 @@ def quantize_tiles(tiles: torch.Tensor, quant_args: dict):
     if not tiles.is_cuda:
         raise ValueError("quantize_tiles requires CUDA tiles (kquant_b200 has no CPU path)")
     bits = int(quant_args["K"])
-    if bits not in (2, 3, 4):
-        raise ValueError("the trellis kernel supports K2--K4")
+    if bits not in TRELLIS_BITS:
+        raise ValueError("the trellis kernels support K1--K8")
     kind, lut = _tile_codebook(quant_args, bits)
     labels = _labels_for(tiles.device, bits, kind, lut)
     ctx = int(quant_args.get("tailbite_context", 128))
@@ -559,14 +564,12 @@ def _ldlq_traverse_steps(weights, Ls, quant_args, plan: _RatePlan, *, buffer_row
 
     progress = 0
     fused = (state is None and source_indices is None and process_begin == 0 and process_end == size_k
-             and plan.uniform is not None and len(quant_args.get("devices", [dev])) == 1
+             and plan.uniform in (2, 3, 4) and len(quant_args.get("devices", [dev])) == 1
              and weights.is_contiguous() and weights.dtype == torch.float32)
     if fused:
         # Fused steps: the Viterbi launch gathers W + comp into tiles and
         # scatters What, E = W - What and the states itself.
         bits = plan.uniform
-        if bits not in (2, 3, 4):
-            raise ValueError("the trellis kernel supports K2--K4")
         ctx = int(quant_args.get("tailbite_context", 128))
         if not 1 <= ctx <= 128:
             raise ValueError("tailbite_context must be in 1..128")
@@ -1832,8 +1835,11 @@ class _ChainMember:
         self.tf32 = bool(quant_args.get("ldlq_tf32", False))
         self.rate = int(quant_args["K"]) if rate is None else rate
         bits = {self.rate} if isinstance(self.rate, int) else set(self.rate[1])
-        if not bits <= {2, 3, 4}:
-            raise ValueError("the trellis kernel supports K2--K4")
+        if not bits <= set(TRELLIS_BITS):
+            raise ValueError("the trellis kernels support K1--K8")
+        # K2..K4 run on the chain kernel; K1 and K5..K8 (uniform only) step by step
+        self.chain_ok = bits <= {2, 3, 4}
+        self.quant_args = quant_args
         self.ctx = int(quant_args.get("tailbite_context", 128))
         if not 1 <= self.ctx <= 128:
             raise ValueError("tailbite_context must be in 1..128")
@@ -1909,23 +1915,93 @@ class _Chain:
                 torch.backends.cuda.matmul.allow_tf32 = previous
 
 
+def _launch_key(c: _Chain):
+    return c.K, c.m.labels[c.K].data_ptr()
+
+
+def _launch_ctas(chains) -> int:
+    """CTAs of a mixed chain launch: one per tile pair up to one pair per SM; beyond, the pairs of each
+    (K, label table), two to a CTA (kq_ldlq_chain_step)."""
+    pairs: dict = {}
+    for c in chains:
+        k = _launch_key(c)
+        pairs[k] = pairs.get(k, 0) + (c.n_tiles + 1) // 2
+    return sum(pairs.values()), sum((p + 1) // 2 for p in pairs.values())
+
+
+def _launch_fits(chains, sms: int) -> bool:
+    pairs, doubled = _launch_ctas(chains)
+    return pairs <= sms or doubled <= sms
+
+
+def _select_launch(cands: list, cap: int, sms: int) -> list:
+    """Chains for one launch, in priority order, within ``cap`` tiles and KQ_CHAIN_MAX_ITEMS items.
+
+    Chains of different K (or codebook) share a launch pair-aligned: every
+    item starts at an even tile (an odd-length chain, an odd run of one K
+    along n, only last) and each CTA runs two pairs of one K, so the pairs of
+    each (K, labels) group, halved and rounded up, must fit the SMs.
+    """
+    sel, tot = [], 0
+    for c in cands:
+        if len(sel) >= _native.KQ_CHAIN_MAX_ITEMS:
+            break
+        if tot + c.n_tiles <= cap or not sel:
+            sel.append(c)
+            tot += c.n_tiles
+    if len({_launch_key(c) for c in sel}) <= 1:
+        return sel
+    evens, odd, tot = [], None, 0
+    for c in cands:
+        if len(evens) + (odd is not None) >= _native.KQ_CHAIN_MAX_ITEMS:
+            break
+        if tot + c.n_tiles > cap and (evens or odd is not None):
+            continue
+        if c.n_tiles % 2:
+            if odd is None and _launch_fits(evens + [c], sms):
+                odd = c
+                tot += c.n_tiles
+        elif _launch_fits(evens + [c] + ([odd] if odd is not None else []), sms):
+            evens.append(c)
+            tot += c.n_tiles
+    return evens + ([odd] if odd is not None else [])
+
+
+def _member_steps(m: _ChainMember) -> None:
+    """LDLQ of a member at a rate the chain kernel does not cover (K1, K5..K8): one launch per 16-row step.
+
+    The steps are those of :func:`_ldlq_traverse_steps` (feedback by FP32
+    GEMM, tile gather, the wide-butterfly Viterbi kernel, scatter), written
+    into the member's own What / codes / feedback arrays.
+    """
+    tiles_n = m.n // 16
+    plan = _RatePlan(int(m.rate), None, 1, tiles_n, m.W.device)
+    _ldlq_traverse(m.W.unsqueeze(0), m.L.unsqueeze(0), m.quant_args, plan, buffer_rows=m.buffer_rows, tf32=m.tf32,
+                   state=(m.wq.unsqueeze(0), m.enc.unsqueeze(0), m.P.unsqueeze(0)))
+
+
 def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None = None, on_buffer=None) -> None:
     """Block-LDLQ of every member (kquant/exl3_encoder_backend.py:389-505 per matrix), fills What and codes.
 
     Each member splits into column chains of at most ``CHAIN_TILES`` tiles
     and one K along the output axis.  Every launch (``kq_ldlq_chain_step``)
     advances a set of chains by one 16-row step: the chains with the most
-    steps left first (the critical path), then any others that fit one wave
-    of 2 x SMs tiles, all with the same tail-biting context; chains of
-    different K share launches.  The kernel computes each step's feedback
+    steps left first (the critical path), then any others that fit, all with
+    the same tail-biting context; chains of different K share launches.  A
+    launch holds up to 4 x SMs tiles (two tile pairs per CTA) while the work
+    left exceeds one wave per critical-path step, then up to 2 x SMs.  The kernel computes each step's feedback
     product itself; the buffer-end feedback updates run between launches on
     the same stream.  ``on_buffer(chain)``, when given, is called when a chain
     is about to start a new 128-row buffer and may return replacement chains
     (the forks of a candidate trie).
     """
     width = chain_tiles or CHAIN_TILES
+    for m in members:
+        if not m.chain_ok:
+            _member_steps(m)
+    members = [m for m in members if m.chain_ok]
     chains = [_Chain(m, c0, nt) for m in members for c0, nt in m.column_runs(width)]
-    cap = 2 * torch.cuda.get_device_properties(device).multi_processor_count
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
     order = {id(c): i for i, c in enumerate(chains)}
     serial = len(chains)
     live = list(chains)
@@ -1948,18 +2024,16 @@ def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None
             live = grown
         live.sort(key=lambda c: (-c.remaining, order[id(c)]))
         ctx = live[0].m.ctx
-        sel, tot = [], 0
-        for c in live:
-            if c.m.ctx != ctx or len(sel) >= _native.KQ_CHAIN_MAX_ITEMS:
-                continue
-            if tot + c.n_tiles <= cap or not sel:
-                sel.append(c)
-                tot += c.n_tiles
-        if len({c.K for c in sel}) > 1:
-            # Items of different K share a launch only pair-aligned: odd-length
-            # chains (an odd run of one K along n) go last, at most one of them.
-            odd = [c for c in sel if c.n_tiles % 2]
-            sel = [c for c in sel if not c.n_tiles % 2] + odd[:1]
+        same = [c for c in live if c.m.ctx == ctx]
+        # Two tile pairs per SM (each CTA hides one pair's tracebacks under the
+        # other's forward steps) while the remaining work exceeds what one-wave
+        # launches along the critical path would cover; one pair per SM after.
+        work = sum(c.n_tiles * c.remaining for c in same)
+        cap = (4 if work > 2 * sms * same[0].remaining else 2) * sms
+        sel = _select_launch(same, cap, sms)
+        if cap > 2 * sms and sum(c.n_tiles for c in sel) < 3.6 * sms:
+            # a launch of two pairs per SM pays only when nearly full
+            sel = _select_launch(same, 2 * sms, sms)
         _native.ldlq_chain_step([c.item() for c in sel], ctx, device)
         for c in sel:
             c.advance()

@@ -79,6 +79,56 @@ def build(ref_root: Path = DEFAULT_REF, force: bool = False) -> Path | None:
     return OUT
 
 
+HARNESS = OUT_DIR / "kquant_ref_harness.so"
+
+
+def build_harness(ref_root: Path = DEFAULT_REF, force: bool = False) -> Path | None:
+    """Compile oracle/ref_harness.cu (the reference's sqg_quantize.cu for every K in 1..8) into oracle/_ref."""
+    if HARNESS.exists() and not force:
+        return HARNESS
+    if not available(ref_root):
+        return None
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    csrc = ref_root / "kquant" / "csrc"
+    OUT_DIR.mkdir(exist_ok=True)
+    incs = [f"-I{p}" for p in ce.include_paths(device_type="cuda")] + [
+        f"-I{sysconfig.get_paths()['include']}", f"-I{csrc}"]
+    abi = f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}"
+    nvcc = os.environ.get("CUDA_HOME", "/usr/local/cuda") + "/bin/nvcc"
+    obj = OUT_DIR / "ref_harness.o"
+    cmd = [nvcc, "-c", str(HERE / "ref_harness.cu"), "-o", str(obj), "-Xcompiler", "-fPIC", "-std=c++17",
+           "-O3", "--use_fast_math", "-lineinfo", "-gencode", "arch=compute_100a,code=sm_100a",
+           "--expt-relaxed-constexpr", "-Xcudafe", "--diag_suppress=177", "-Xcudafe", "--diag_suppress=20012",
+           "-D__CUDA_NO_HALF_OPERATORS__", "-D__CUDA_NO_HALF_CONVERSIONS__", "-D__CUDA_NO_HALF2_OPERATORS__",
+           "-D__CUDA_NO_BFLOAT16_CONVERSIONS__", "-DTORCH_EXTENSION_NAME=kquant_ref_harness",
+           "-DTORCH_API_INCLUDE_EXTENSION_H", abi, *incs]
+    subprocess.run(cmd, check=True)
+    libdir = Path(torch.__file__).parent / "lib"
+    link = ["g++", "-shared", "-o", str(HARNESS), str(obj), f"-L{libdir}", "-lc10", "-lc10_cuda", "-ltorch",
+            "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+            f"-L{os.environ.get('CUDA_HOME', '/usr/local/cuda')}/lib64", "-lcudart", f"-Wl,-rpath,{libdir}"]
+    subprocess.run(link, check=True)
+    obj.unlink(missing_ok=True)
+    return HARNESS
+
+
+def load_harness():
+    """ctypes handle of the compiled harness (needs `import torch` first)."""
+    import ctypes
+    import torch  # noqa: F401
+    if not HARNESS.exists():
+        raise FileNotFoundError(f"{HARNESS} not built")
+    lib = ctypes.CDLL(str(HARNESS))
+    P, I = ctypes.c_void_p, ctypes.c_int
+    lib.kqref_quantize_procedural.argtypes = [P, P, P, P, P, I, I, I, I, I, P]
+    lib.kqref_quantize_procedural.restype = I
+    lib.kqref_decision_bytes_per_tile.argtypes = [I]
+    lib.kqref_decision_bytes_per_tile.restype = ctypes.c_longlong
+    return lib
+
+
 def load():
     """Import the compiled reference extension (needs `import torch` first)."""
     import importlib.util
@@ -93,5 +143,6 @@ def load():
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    path = build(Path(args[0]) if args else DEFAULT_REF, force="--force" in sys.argv)
-    print(path)
+    root = Path(args[0]) if args else DEFAULT_REF
+    print(build(root, force="--force" in sys.argv))
+    print(build_harness(root, force="--force" in sys.argv))

@@ -63,11 +63,46 @@ def load_reference_backend(ref_root: Path):
         m.__dict__.update(vars(mod))
         sys.modules[name] = m
     module = load_qsrt_encoder(Path(tempfile.mkdtemp()))
+    if build_ref.HARNESS.exists():
+        module.quantize_tiles = _procedural_quantizer(build_ref.load_harness())
     ext = build_ref.load()
     sqg_quantizer._extension = lambda: ext
     sqg_quantizer.install_sqg_quantizer(module)
     module.pack_trellis = lambda enc, qa: qsrt.pack_trellis_edges(enc, qa["K"])
     return module
+
+
+def _procedural_quantizer(harness):
+    """The reference backend's plain (non-SQG) tile quantiser, served by the reference kernel template at any K.
+
+    Upstream EXL3 calls ext.quantize_tiles with the MCG / MUL1 flags taken from
+    the key presence of ``mcg`` / ``mul1`` (kquant/exl3_encoder_backend.py:81-111);
+    that extension is not vendored, so the reference's own kernel
+    (oracle/ref_harness.cu) stands in for it.
+    """
+    def quantize_tiles(tiles, quant_args):
+        if "mcg" in quant_args:
+            cb = 1
+        elif "mul1" in quant_args:
+            cb = 2
+        else:
+            raise NotImplementedError("3INST tiles have no reference kernel here")
+        tiles = tiles.contiguous()
+        K, n, dev = int(quant_args["K"]), tiles.shape[0], tiles.device
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        mb = max(1, min(n, sms))
+        costs = torch.zeros((mb, 2, 65536 >> K), dtype=torch.float16, device=dev)
+        edges = torch.empty(mb * harness.kqref_decision_bytes_per_tile(K), dtype=torch.uint8, device=dev)
+        out = torch.empty_like(tiles)
+        idx = torch.empty((n, 256), dtype=torch.int16, device=dev)
+        rc = harness.kqref_quantize_procedural(tiles.data_ptr(), out.data_ptr(), idx.data_ptr(), costs.data_ptr(),
+                                               edges.data_ptr(), n, mb, K, cb,
+                                               int(quant_args.get("tailbite_context", 128)),
+                                               torch.cuda.current_stream(dev).cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"reference harness failed: {rc}")
+        return out, idx
+    return quantize_tiles
 
 
 def _states(module_qsrt, trellis, K):

@@ -15,6 +15,10 @@ Shapes follow the benchmark configurations of the encode path:
 * ``cfg1_slice_7168_k3``: a 256-column slice of the gate projection of one
   expert triplet (EXL k = 7168: 448 LDLQ steps, 56 buffers), Student-t rows,
   H from 8192 tokens, K=3.
+* ``mla_kvb_slice_k5``: a 1024-column slice of an MLA kv_b_proj (EXL k = 512)
+  at K=5 on the procedural MCG codebook, H from 2048 tokens.  The reference
+  host rejects K=5, so its tile quantiser here is the reference kernel
+  template launched at K=5 (oracle/ref_harness.cu).
 * ``batch_n_r012`` / ``batch_k_r012``: kquant's production call
   ``quantize_qsrt_batch`` over two sources x the rate-transfer modes
   R0/R1/R2, along n (gate-like, the n-axis candidate reuse) and along k
@@ -33,6 +37,9 @@ from kquant_b200.codebooks import sqg_xor_cheb_t12_bytes
 QSRT_CASES = {
     "cfg0_2048_k4": {"kind": "dense", "k": 2048, "n": 2048, "K": 4, "tokens": 4096, "seed": 21},
     "cfg1_slice_7168_k3": {"kind": "triplet_slice", "k": 7168, "n": 256, "K": 3, "tokens": 8192, "seed": 22},
+    # MLA kv_b_proj-like slice (EXL k = 512 latent rows) at K=5 on the procedural MCG codebook
+    "mla_kvb_slice_k5": {"kind": "dense", "k": 512, "n": 1024, "K": 5, "tokens": 2048, "seed": 23,
+                         "codebook": "mcg"},
 }
 
 BATCH_CASES = {
@@ -81,10 +88,14 @@ def _student_rows(g: torch.Generator, rows: int, cols: int, std: float) -> torch
     return w * (t.abs() / t.abs().median()).unsqueeze(1)
 
 
-def base_args(K: int, seed: int, device) -> dict:
-    return {"K": K, "seed": 1000 + seed, "sv_seed": 2000 + seed, "sigma_reg": 0.025, "devices": [str(device)],
-            "apply_out_scales": None, "tailbite_context": 128,
-            "sqg_e4m3_luts_by_bits": {b: sqg_xor_cheb_t12_bytes(b) for b in (2, 3, 4)}}
+def base_args(K: int, seed: int, device, codebook: str = "sqg") -> dict:
+    args = {"K": K, "seed": 1000 + seed, "sv_seed": 2000 + seed, "sigma_reg": 0.025, "devices": [str(device)],
+            "apply_out_scales": None, "tailbite_context": 128}
+    if codebook == "sqg":
+        args["sqg_e4m3_luts_by_bits"] = {b: sqg_xor_cheb_t12_bytes(b) for b in (2, 3, 4)}
+    else:
+        args[codebook] = True
+    return args
 
 
 def qsrt_inputs(name: str, device):
@@ -103,7 +114,7 @@ def qsrt_inputs(name: str, device):
         w = _student_rows(g, n, k, 0.015).to(torch.bfloat16).float().T.contiguous()
         x = torch.randn((c["tokens"], k), generator=g) * torch.exp(torch.randn(k, generator=g))
         h = _hessian(x, device, None)
-    return w.to(device), h, base_args(c["K"], c["seed"], device)
+    return w.to(device), h, base_args(c["K"], c["seed"], device, c.get("codebook", "sqg"))
 
 
 def batch_inputs(name: str, device):

@@ -310,3 +310,42 @@ def test_mixed_chain_engine_odd_runs(cuda_device):
     wq_o, enc_o = _old_path(W, Ls, qal)
     assert torch.equal(enc_c, enc_o)
     assert torch.equal(wq_c, wq_o)
+
+
+@pytest.mark.parametrize("rates", [(3, 3, 3, 3), (2, 3, 4, 3)])
+def test_double_wave_chain_launches_equal_single_wave(cuda_device, monkeypatch, rates):
+    """Launches of two tile pairs per CTA (uniform K: the grid-stride kernel; mixed K: the per-CTA pair table)
+    give the same codes and What, bit for bit, as one-wave launches of the same chains."""
+    dev = cuda_device
+    k, n = 512, 2048
+
+    def run():
+        members, outs = [], []
+        for b, K in enumerate(rates):
+            w, h = _problem(dev, k=k, n=n, seed=80 + b)
+            L, _ = be.block_ldl(h.clone(), 16, {"devices": [str(dev)], "sigma_reg": 0.025}, False)
+            wq = torch.empty_like(w)
+            enc = torch.empty((k // 16, n // 16, 256), dtype=torch.int16, device=dev)
+            members.append(be._ChainMember((w * 25).contiguous(), L, wq, enc, _args(dev, K=K)))
+            outs.append((wq, enc))
+        be._chain_traverse(members, dev)
+        torch.cuda.synchronize()
+        return outs
+
+    sizes = []
+    real_step = _native.ldlq_chain_step
+
+    def spy(items, ctx, device, max_ctas=0):
+        sizes.append(sum(int(i.n_tiles) for i in items))
+        return real_step(items, ctx, device, max_ctas)
+
+    monkeypatch.setattr(_native, "ldlq_chain_step", spy)
+    double = run()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    assert max(sizes) > 2 * sms
+    real_select = be._select_launch
+    monkeypatch.setattr(be, "_select_launch", lambda cands, cap, s: real_select(cands, min(cap, 2 * s), s))
+    single = run()
+    for (wq_d, enc_d), (wq_s, enc_s) in zip(double, single):
+        assert torch.equal(enc_d, enc_s)
+        assert torch.equal(wq_d, wq_s)

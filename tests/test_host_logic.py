@@ -125,3 +125,22 @@ def test_sample_scale_tiles_shape_and_order():
 def test_no_cpu_path():
     with pytest.raises(ValueError, match="CUDA"):
         be.quantize_tiles(torch.zeros(1, 256), {"K": 3, "devices": ["cpu"], "mcg": True})
+
+
+@pytest.mark.parametrize("k,n", [(7168, 2048), (2048, 7168), (2048, 2048), (128, 256), (512, 1024)])
+def test_tile_encode_count_matches_scale_search_sampling(k, n):
+    """bench.tile_encodes (the CPU arm's scale-search charge) equals the encodes the backend performs."""
+    import bench
+    w = torch.randn((k, n))
+    samples = be.sample_scale_tiles(w).shape[0]
+    assert bench.tile_encodes(k, n) == (k // 16) * (n // 16) + 10 * len(range(0, samples, 3)) + 5 * samples
+
+
+def test_layer_rate_allocation_is_3p2_bpw_and_seeded():
+    import bench
+    ks = bench.layer_rates()
+    flat = [k for row in ks for k in row]
+    assert len(ks) == bench.LAYER_EXPERTS + 1 and all(len(r) == 3 for r in ks)
+    assert {k: flat.count(k) for k in (2, 3, 4)} == {2: 231, 3: 462, 4: 462}
+    assert sum(flat) / len(flat) == pytest.approx(3.2)
+    assert bench.layer_rates() == ks and bench.layer_rates(seed=1) != ks

@@ -87,3 +87,17 @@ def test_oracle_viterbi_closes_cyclic_paths(oracle_mod):
         edges = (idx & ((1 << K) - 1)).astype(np.int16)
         assert np.array_equal(O.reconstruct_states(edges, K).view(np.uint16), idx)
         assert np.array_equal(val, lab[idx].view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("K", [1, 5, 8])
+def test_oracle_wide_rates_give_closed_cyclic_paths(oracle_mod, K):
+    """K outside 2..4 (the reference template's other rates): every encoded tile is a closed cyclic
+    trellis path, state_i = ((state_{i-1} << K) | edge_i) & 0xFFFF, and values are its labels."""
+    O = oracle_mod
+    lab = O.labels(O.CB_MCG)
+    tiles = np.random.default_rng(K).standard_normal((2, 256)).astype(np.float32)
+    idx, val, rc = O.viterbi(K, lab, tiles, 32)
+    assert rc == 0
+    edges = (idx & ((1 << K) - 1)).astype(np.int16)
+    assert np.array_equal(O.reconstruct_states(edges, K).view(np.uint16), idx)
+    assert np.array_equal(val, lab[idx].view(np.float16).astype(np.float32))

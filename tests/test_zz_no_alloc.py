@@ -42,7 +42,9 @@ def test_noalloc_matches_workspace_entry_point_twice(native, cuda_device):
     L = native.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
     g = torch.Generator(device=cuda_device).manual_seed(2024)
-    cases = [(3, 600, 128), (4, 37, 64)]          # second call: other K, odd count, other context
+    # two calls in a row (other K, odd count, other context), then: one tile and one pair (a single job per
+    # CTA, half a pair), K2, and the per-call bound of 4096 tiles
+    cases = [(3, 600, 128), (4, 37, 64), (3, 1, 128), (4, 2, 16), (2, 300, 128), (3, 4096, 128)]
     for K, n, C in cases:
         tiles = torch.randn((n, 256), generator=g, device=cuda_device)
         tiles[: n // 3] = torch.round(tiles[: n // 3] * 2) / 2      # tie-heavy tiles
