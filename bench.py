@@ -136,9 +136,10 @@ class Layer:
     The shared expert (index 384) sees all 8192 tokens.
     """
 
-    def __init__(self, device: torch.device, experts: list[int], seed: int = 77):
+    def __init__(self, device: torch.device, experts: list[int], seed: int = 77, layer: int = 0):
         self.device = device
-        self.rates = layer_rates()
+        self.layer = layer
+        self.rates = layer_rates(78 + layer)
         g = torch.Generator(device=device).manual_seed(seed)
         chan = torch.exp(torch.randn(HIDDEN, generator=g, device=device))
         x_all = torch.randn((TOKENS, HIDDEN), generator=g, device=device) * chan
@@ -147,7 +148,7 @@ class Layer:
         routed.scatter_(1, logits.topk(TOP_K, dim=1).indices, True)
         self.experts = []
         for e in experts:
-            (gate, up, down), _, _ = make_triplet_weights(device, seed=5000 + e)
+            (gate, up, down), _, _ = make_triplet_weights(device, seed=5000 + 1000 * layer + e)
             if e == SHARED:
                 x = x_all
             else:
@@ -168,7 +169,8 @@ class Layer:
         out = []
         for e, (ws, h13, h2) in exl.items():
             ks = self.rates[e]
-            qa = [quant_args(m, self.device, layer=e + 1, K=k) for m, k in zip(("w1", "w3", "w2"), ks)]
+            qa = [quant_args(m, self.device, layer=1000 * self.layer + e + 1, K=k)
+                  for m, k in zip(("w1", "w3", "w2"), ks)]
             s13 = make_shared_h(HIDDEN, self.device, h13)
             if ks[0] == ks[1]:
                 out.append(([ws[0], ws[1]], [s13, s13], qa[:2]))
@@ -974,6 +976,77 @@ def run_layer_case(args, world, rank, local):
                           "clocks": clk.summary(), "data": "synthetic"}), flush=True)
 
 
+def run_stream_case(args, world, rank, local):
+    """configs[4]-style streaming: --layers consecutive MoE layers, each rank encoding --experts experts of its
+    shard of every layer.  Layer l+1's synthetic weights and Hessians are generated on the device, from a seed,
+    on a side stream while layer l encodes; each layer's packed trellis and scales go back to pinned host
+    memory on a third stream.  Reports sustained encoded weights/s over the whole stream (device events,
+    max over ranks)."""
+    from kquant_b200 import _native
+    from kquant_b200 import exl3_encoder_backend as be
+    from kquant_b200.sharding import shard_experts
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _native.load()
+    main_stream = torch.cuda.current_stream(device)
+    gen_stream, out_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    mine = shard_experts([1.0] * LAYER_EXPERTS, world, rank)[:args.experts]
+
+    def generate(layer):
+        with torch.cuda.stream(gen_stream):
+            lay = Layer(device, mine, layer=layer)
+            exl = {e: ([to_exl(w) for w in hf], h13, h2) for e, hf, h13, h2 in lay.experts}
+            ready = gen_stream.record_event()
+        return lay, exl, ready
+
+    warm = Layer(device, mine[:1], layer=args.layers)        # warm-up: one expert of a layer outside the stream
+    warm.encode()
+    del warm
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    host_out, pending = [], []
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        a.record()
+        nxt = generate(0)
+        for layer in range(args.layers):
+            lay, exl, ready = nxt
+            main_stream.wait_event(ready)
+            for ws, h13, h2 in exl.values():
+                for t in (*ws, h13, h2):
+                    t.record_stream(main_stream)
+            if layer + 1 < args.layers:
+                nxt = generate(layer + 1)
+            res = be.quantize_uniform_batches(lay.groups(exl))
+            done = main_stream.record_event()
+            with torch.cuda.stream(out_stream):
+                out_stream.wait_event(done)
+                for grp in res:
+                    for _, tens in grp:
+                        for v in tens.values():
+                            v.record_stream(out_stream)
+                            dst = torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+                            dst.copy_(v, non_blocking=True)
+                            host_out.append(dst)
+            pending.append(res)
+        main_stream.wait_stream(out_stream)
+        b.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    t = _allreduce_max(a.elapsed_time(b) / 1e3, world)
+    weights = args.layers * len(mine) * 3 * HIDDEN * INTER * world
+    proxies = [p for res in pending for grp in res for p, _ in grp]
+    if rank == 0:
+        print(json.dumps({"case": "stream", "layers": args.layers, "experts_per_gpu_per_layer": len(mine),
+                          "n_gpus": world, "weights": weights, "wall_s": t,
+                          "sustained_mweights_per_s": weights / t / 1e6,
+                          "d2h_bytes": sum(x.numel() * x.element_size() for x in host_out),
+                          "proxy_max": max(proxies), "clocks": clk.summary(),
+                          "data": "synthetic, generated on the device per layer"}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -984,7 +1057,7 @@ def main():
     ap.add_argument("--no-per-k", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--case", default="slice",
-                    choices=["slice", "triplet", "layer", "qsrt", "chain", "viterbi", "microbench", "mla", "trace",
+                    choices=["slice", "triplet", "layer", "stream", "qsrt", "chain", "viterbi", "microbench", "mla", "trace",
                              "pack", "load", "hessian", "profile"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=None, help="viterbi: 1184; microbench: 1,048,576")
@@ -993,6 +1066,7 @@ def main():
     ap.add_argument("--dim", type=int, default=HIDDEN, help="hessian case: sample width")
     ap.add_argument("--experts", type=int, default=4, help="slice: experts per GPU; layer: experts per batch")
     ap.add_argument("--top", type=int, default=25, help="profile case: kernels listed")
+    ap.add_argument("--layers", type=int, default=8, help="stream case: consecutive layers")
     args = ap.parse_args()
     if args.tiles is None:
         args.tiles = 1 << 20 if args.case == "microbench" else 1184
@@ -1008,6 +1082,8 @@ def main():
         run_reference(args, world, rank)
     elif args.case == "layer":
         run_layer_case(args, world, rank, local)
+    elif args.case == "stream":
+        run_stream_case(args, world, rank, local)
     else:
         run_encode(args, world, rank, local)
     if world > 1:

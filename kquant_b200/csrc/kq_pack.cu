@@ -53,11 +53,28 @@ __global__ void unpack_states_kernel(const uint16_t* __restrict__ packed, int64_
     const int64_t tile = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (tile >= n) return;                   // whole warps exit together
-    const uint16_t* src = packed + tile * 16 * K;
+    // The tile's 16K words are 8K 32-bit words: lanes 0..8K-1 load one each
+    // (coalesced), then every lane gathers its group's K stream words by
+    // shuffles.  Stream word w of group g is packed word (g K + w) ^ 1 (SWAP16).
+    const uint32_t* src32 = reinterpret_cast<const uint32_t*>(packed + tile * 16 * K);
+    uint32_t mine32 = 0;
+    if (lane < 8 * K) mine32 = __ldcs(src32 + lane);
+    uint32_t more32 = 0;                     // K > 4: 8K > 32 words, lanes take a second one
+    if (K > 4 && lane + 32 < 8 * K) more32 = __ldcs(src32 + 32 + lane);
     const int g = lane >> 1, half = lane & 1;
     uint32_t win[K + 1];
 #pragma unroll
-    for (int w = 0; w < K; ++w) win[w] = __ldcs(src + ((g * K + w) ^ 1));
+    for (int w = 0; w < K; ++w) {
+        const int idx = (g * K + w) ^ 1;     // 16-bit word index in the tile
+        const int j = idx >> 1;              // its 32-bit word
+        const uint32_t lo = __shfl_sync(0xFFFFFFFFu, mine32, j & 31);
+        uint32_t v = lo;
+        if (K > 4) {
+            const uint32_t hi = __shfl_sync(0xFFFFFFFFu, more32, j & 31);
+            v = (j >= 32) ? hi : lo;
+        }
+        win[w] = (idx & 1) ? (v >> 16) : (v & 0xFFFFu);
+    }
     uint32_t e[8];
     const uint32_t mask = (1u << K) - 1u;
 #pragma unroll
@@ -128,6 +145,7 @@ int unpack_trellis_states(const uint16_t* packed, int64_t n, int K, uint16_t* st
     if (n < 0 || (n > 0 && (!states || !packed))) { set_error("unpack_trellis: bad arguments"); return KQ_ERR_ARG; }
     if (n == 0) return KQ_OK;
     if ((uintptr_t)states & 15) { set_error("unpack_trellis: states must be 16-byte aligned"); return KQ_ERR_ALIGN; }
+    if ((uintptr_t)packed & 3) { set_error("unpack_trellis: packed must be 4-byte aligned"); return KQ_ERR_ALIGN; }
     const int64_t threads = n * 32;
     const unsigned grid = (unsigned)((threads + 255) / 256);
     switch (K) {

@@ -51,12 +51,15 @@ struct WideMap {
     static constexpr int NW = (NP + SLOTS - 1) / SLOTS;      // decision words per thread per step
     static constexpr int ROW_WORDS = NW * kWThreads;
     static constexpr int ROW_BYTES = ROW_WORDS * 4;
-    static constexpr int PADDED = NODES + 2 * (NODES >> 6);  // cost entries with 2 pad halves per 64
+    static constexpr bool PAD = SP > 1;                      // padded cost layout (split predecessors)
+    static constexpr int PADDED = PAD ? NODES + 2 * (NODES >> 6) : NODES;
     static_assert(NP * QT == 64 && G * PBW == NP && CH * S == QT, "ownership");
 
-    // Shared-memory index of node e's cost (2 pad halves every 64 nodes keep
-    // the split-predecessor loads of K7/K8 on distinct banks).
-    __host__ __device__ static constexpr int pad(int e) { return e + ((e >> 6) << 1); }
+    // Shared-memory index of node e's cost.  With split predecessors (K7, K8)
+    // 2 pad halves every 64 nodes keep the SP threads' loads on distinct banks;
+    // otherwise the layout is plain, so every load and store of a step is a
+    // per-thread base plus a compile-time offset.
+    __host__ __device__ static constexpr int pad(int e) { return PAD ? e + ((e >> 6) << 1) : e; }
 
     // Block index h (= e >> K) of group g of thread tid and its first pair.
     __device__ static __forceinline__ void block_of(int tid, int g, int& h, int& pair0) {
@@ -119,6 +122,10 @@ __device__ __forceinline__ void wide_step(const half2 (&L)[WideMap<K>::NP][WideM
         M::block_of(tid, g, h, pair0);
         half2 mn[M::PBW][M::S];
         uint32_t id[M::PBW][M::S];
+        // Predecessor (kbase + kk) << DSHIFT | h sits at cbase + pad(kk << DSHIFT):
+        // kbase << DSHIFT is a multiple of 64 and h < 2^DSHIFT, so the padding
+        // splits into a per-thread part and a compile-time part.
+        const __half* cbase = cprev + M::pad(kbase << M::DSHIFT) + h;
 #pragma unroll
         for (int j = 0; j < M::CH; ++j) {
 #pragma unroll
@@ -126,7 +133,7 @@ __device__ __forceinline__ void wide_step(const half2 (&L)[WideMap<K>::NP][WideM
                 const int kk = s * M::CH + j;
                 const int pk = ((kbase + kk) << M::DSHIFT) | h;
                 half2 c2;
-                if constexpr (STEP0 == 0) c2 = __half2half2(cprev[M::pad(pk)]);
+                if constexpr (STEP0 == 0) c2 = __half2half2(cbase[M::pad(kk << M::DSHIFT)]);
                 else if constexpr (STEP0 == 1) c2 = zero2;
                 else c2 = (pk == es) ? zero2 : inf2;
 #pragma unroll

@@ -164,8 +164,16 @@ def quantize_tiles(tiles: torch.Tensor, quant_args: dict):
     return _native.viterbi_encode(tiles, bits, labels, ctx)
 
 
-@lru_cache
 def get_quant_stream(device):
+    """The quantizer's stream of a device (one per device, however the device is named)."""
+    d = torch.device(device)
+    if d.index is None:
+        d = torch.device(d.type, torch.cuda.current_device())
+    return _quant_stream(d)
+
+
+@lru_cache
+def _quant_stream(device: torch.device):
     return torch.cuda.Stream(device=device)
 
 
@@ -618,8 +626,15 @@ def _ldlq_traverse_steps(weights, Ls, quant_args, plan: _RatePlan, *, buffer_row
 
 
 def _sync(devices):
+    """Host waits for the calling stream and the quantizer stream of each device.
+
+    The reference synchronises whole devices (kquant/exl3_encoder_backend.py:418-420);
+    this build only orders the two streams its work runs on, so unrelated work on
+    other streams of the same device (data generation, copies) keeps overlapping.
+    """
     for d in devices:
-        torch.cuda.synchronize(d)
+        torch.cuda.current_stream(d).synchronize()
+        get_quant_stream(d).synchronize()
 
 
 def _buffer_rows(quant_args: dict, size_k: int) -> int:

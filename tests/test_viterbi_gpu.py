@@ -107,3 +107,22 @@ def test_viterbi_matches_reference_kernel(native, ref_ext, cuda_device, K, C):
     torch.cuda.synchronize()
     assert torch.equal(states, ref_idx)
     assert torch.equal(vals, ref_out)
+
+
+@pytest.mark.parametrize("K", [2, 3, 4, 1, 5])
+def test_all_infinite_primer_costs_give_a_closed_path(native, cuda_device, K):
+    """|w| >= 300 overflows every binary16 cost to +inf.  The reference argmin then returns -1 and reads
+    outside its decision buffer (qsrt_quantize_tiles_kernel.cuh:330-413), so the reference is not run here;
+    this build takes the first node in the reference's tie order and must still emit a closed cyclic path
+    whose values are the labels of its states."""
+    kind = 4 if K in (2, 3, 4) else 1
+    lut = cb.sqg_xor_cheb_t12_bytes(K).to(cuda_device) if kind == 4 else None
+    lab = native.build_labels(kind, lut, cuda_device)
+    tiles = torch.full((3, 256), 1000.0, device=cuda_device)
+    tiles[1] = -700.0
+    vals, states = native.viterbi_encode(tiles, K, lab, 128)
+    torch.cuda.synchronize()
+    st = states.long() & 0xFFFF
+    prev = torch.roll(st, 1, dims=1)
+    assert torch.equal(((prev << K) | (st & ((1 << K) - 1))) & 0xFFFF, st)
+    assert torch.equal(vals, lab[st].view(torch.float16).float())
