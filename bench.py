@@ -548,7 +548,7 @@ def run_pack_case(args, local):
     from kquant_b200 import _native
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    n = weights_per_step() // 256
+    n = 3 * HIDDEN * INTER // 256
     K = args.K
     states = torch.randint(-32768, 32767, (n, 256), dtype=torch.int16, device=device)
     packed = _native.pack_trellis(states, K)

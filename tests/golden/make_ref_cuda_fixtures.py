@@ -68,8 +68,19 @@ def load_reference_backend(ref_root: Path):
     ext = build_ref.load()
     sqg_quantizer._extension = lambda: ext
     sqg_quantizer.install_sqg_quantizer(module)
-    module.pack_trellis = lambda enc, qa: qsrt.pack_trellis_edges(enc, qa["K"])
+    module.pack_trellis = _pack_any_k
     return module
+
+
+def _pack_any_k(enc, qa):
+    """pack_trellis stub: kquant.qsrt's restatement for K2..K4 (the only rates it accepts); the C oracle's
+    restatement of the same word order (oracle/kq_oracle.c) at other K."""
+    from kquant import qsrt
+    K = int(qa["K"])
+    if K in (2, 3, 4):
+        return qsrt.pack_trellis_edges(enc, K)
+    from oracle import oracle as O
+    return torch.from_numpy(O.pack_trellis(enc.cpu().numpy(), K)).to(enc.device)
 
 
 def _procedural_quantizer(harness):
@@ -106,7 +117,11 @@ def _procedural_quantizer(harness):
 
 
 def _states(module_qsrt, trellis, K):
-    return module_qsrt.unpack_trellis_states(trellis.cpu(), K).to(torch.int16)
+    if K in (2, 3, 4):
+        return module_qsrt.unpack_trellis_states(trellis.cpu(), K).to(torch.int16)
+    from oracle import oracle as O
+    edges = O.unpack_trellis(trellis.cpu().numpy(), K)
+    return torch.from_numpy(O.reconstruct_states(edges, K)).to(torch.int16)
 
 
 def run_qsrt_case(name, ref, kq, device):
