@@ -1982,17 +1982,48 @@ def _select_launch(cands: list, cap: int, sms: int) -> list:
     return evens + ([odd] if odd is not None else [])
 
 
-def _member_steps(m: _ChainMember) -> None:
-    """LDLQ of a member at a rate the chain kernel does not cover (K1, K5..K8): one launch per 16-row step.
+def _member_step_gen(m: _ChainMember):
+    tiles_n = m.n // 16
+    plan = _RatePlan(int(m.rate), None, 1, tiles_n, m.W.device)
+    return _ldlq_traverse_steps(m.W.unsqueeze(0), m.L.unsqueeze(0), m.quant_args, plan, buffer_rows=m.buffer_rows,
+                                tf32=m.tf32, state=(m.wq.unsqueeze(0), m.enc.unsqueeze(0), m.P.unsqueeze(0)))
+
+
+def _members_steps(ms: list) -> None:
+    """LDLQ of members at rates the chain kernel does not cover (K1, K5..K8): one launch per 16-row step.
 
     The steps are those of :func:`_ldlq_traverse_steps` (feedback by FP32
     GEMM, tile gather, the wide-butterfly Viterbi kernel, scatter), written
-    into the member's own What / codes / feedback arrays.
+    into each member's own What / codes / feedback arrays.  Several members
+    advance in turn, each on its own stream, so one member's last partial
+    wave of tiles shares the GPU with the others' launches; every member's
+    arithmetic is unchanged.
     """
-    tiles_n = m.n // 16
-    plan = _RatePlan(int(m.rate), None, 1, tiles_n, m.W.device)
-    _ldlq_traverse(m.W.unsqueeze(0), m.L.unsqueeze(0), m.quant_args, plan, buffer_rows=m.buffer_rows, tf32=m.tf32,
-                   state=(m.wq.unsqueeze(0), m.enc.unsqueeze(0), m.P.unsqueeze(0)))
+    if not ms:
+        return
+    if len(ms) == 1:
+        _drive(_member_step_gen(ms[0]))
+        return
+    cur = torch.cuda.current_stream(ms[0].W.device)
+    live = []
+    for m in ms:
+        st = torch.cuda.Stream(device=m.W.device)
+        st.wait_stream(cur)
+        with torch.cuda.stream(st):
+            live.append((st, _member_step_gen(m)))
+    streams = [st for st, _ in live]
+    while live:
+        nxt = []
+        for st, gen in live:
+            with torch.cuda.stream(st):
+                try:
+                    next(gen)
+                    nxt.append((st, gen))
+                except StopIteration:
+                    pass
+        live = nxt
+    for st in streams:
+        cur.wait_stream(st)
 
 
 def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None = None, on_buffer=None) -> None:
@@ -2011,9 +2042,7 @@ def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None
     (the forks of a candidate trie).
     """
     width = chain_tiles or CHAIN_TILES
-    for m in members:
-        if not m.chain_ok:
-            _member_steps(m)
+    _members_steps([m for m in members if not m.chain_ok])
     members = [m for m in members if m.chain_ok]
     chains = [_Chain(m, c0, nt) for m in members for c0, nt in m.column_runs(width)]
     sms = torch.cuda.get_device_properties(device).multi_processor_count

@@ -126,3 +126,39 @@ def test_wide_rate_ldlq_matches_unfused_reference_order(native, cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(enc, ref_enc)
     assert torch.equal(wq, ref_wq)
+
+
+def test_wide_rate_members_on_streams_equal_single_runs(native, cuda_device):
+    """Several K1/K5..K8 members of one engine run (stepped in turn on their own streams) give the same codes
+    and What, bit for bit, as each member run alone."""
+    from kquant_b200 import exl3_encoder_backend as be
+    g = torch.Generator(device=cuda_device).manual_seed(6)
+    shapes = [(256, 512, 5), (128, 1024, 6), (384, 256, 1)]
+
+    def make():
+        out = []
+        for k, n, K in shapes:
+            W = torch.randn((k, n), generator=g, device=cuda_device) * 0.5
+            L = torch.tril(torch.randn((k, k), generator=g, device=cuda_device) * 0.02, -1)
+            out.append((W, L, K))
+        return out
+
+    probs = make()
+
+    def member(W, L, K):
+        args = {"K": K, "mcg": True, "devices": [str(cuda_device)], "tailbite_context": 64}
+        k, n = W.shape
+        return be._ChainMember(W, L, torch.empty_like(W), torch.empty((k // 16, n // 16, 256), dtype=torch.int16,
+                                                                      device=cuda_device), args)
+
+    together = [member(*p) for p in probs]
+    be._chain_traverse(together, cuda_device)
+    alone = []
+    for p in probs:
+        m = member(*p)
+        be._chain_traverse([m], cuda_device)
+        alone.append(m)
+    torch.cuda.synchronize()
+    for a, b in zip(together, alone):
+        assert torch.equal(a.enc, b.enc)
+        assert torch.equal(a.wq, b.wq)
