@@ -135,7 +135,7 @@ typedef struct {
     int32_t reserved;         /* 0 */
 } kq_chain_item;
 
-#define KQ_CHAIN_MAX_ITEMS 32
+#define KQ_CHAIN_MAX_ITEMS 64
 
 /*
  * One launch of LDLQ steps from up to KQ_CHAIN_MAX_ITEMS independent column
@@ -152,10 +152,10 @@ typedef struct {
  * Items carry their own K and label table.  When they all share both the
  * launch may hold any number of tiles.  Items of different K (or label
  * tables) share a launch when every item starts at an even tile (so each
- * tile pair has one K) and either the launch has at most one pair per SM
- * (one pair per CTA) or the pairs of each (K, labels) group, two to a CTA,
- * need at most one CTA per SM; a CTA with two pairs hides each pair's
- * tracebacks under the other's forward steps.  Workspace as
+ * tile pair has one K) and the pairs of each (K, labels) group, in runs of
+ * m per CTA (m from ceil(pairs / SMs) up to 4), need at most one CTA per SM;
+ * a CTA with two or more pairs hides each pair's tracebacks under another's
+ * forward steps.  Workspace as
  * kq_viterbi_encode (K = 3) for the total tile count; max_ctas as
  * kq_ldlq_step_encode.
  */

@@ -42,7 +42,7 @@ EXPORTED = (
     "kq_ldlq_chain_step",
 )
 
-KQ_CHAIN_MAX_ITEMS = 32
+KQ_CHAIN_MAX_ITEMS = 64
 
 
 class ChainItem(ctypes.Structure):

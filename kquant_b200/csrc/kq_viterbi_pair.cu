@@ -36,6 +36,7 @@ constexpr int kThreads = 512;
 constexpr int kJobs = 2;
 constexpr int kStageBufs = 4;   // traceback row staging: buffers in the cp.async pipeline
 constexpr int kMaxChainCtas = 160;   // CTAs of a mixed-K chain launch (one per SM)
+constexpr int kMaxCtaPairs = 4;      // tile pairs per CTA of a mixed-K chain launch
 
 template <int K>
 struct PairMap {
@@ -289,8 +290,8 @@ struct ChainIO {
     kq_chain_item it[KQ_CHAIN_MAX_ITEMS];
     int64_t start[KQ_CHAIN_MAX_ITEMS + 1];
     int n;
-    // Mixed-K launches: the tile pairs of CTA b (-1: none); both of one K.
-    int16_t cta_pair[kMaxChainCtas][kJobs];
+    // Mixed-K launches: the tile pairs of CTA b in order (-1: none), all of one K.
+    int16_t cta_pair[kMaxChainCtas][kMaxCtaPairs];
     __device__ __forceinline__ int find(int64_t tile) const {
         int i = 0;
         while (i + 1 < n && tile >= start[i + 1]) ++i;
@@ -390,10 +391,10 @@ constexpr size_t kMaxRowBytes =
         ? (PairMap<2>::ROW_BYTES > PairMap<4>::ROW_BYTES ? PairMap<2>::ROW_BYTES : PairMap<4>::ROW_BYTES)
         : (PairMap<3>::ROW_BYTES > PairMap<4>::ROW_BYTES ? PairMap<3>::ROW_BYTES : PairMap<4>::ROW_BYTES);
 
-// Chain launch whose items may differ in K: each CTA runs one or two tile
+// Chain launch whose items may differ in K: each CTA runs one to four tile
 // pairs of one K (the host's per-CTA pair table, io.cta_pair), with the body
-// for that K and that item's labels.  Two pairs per CTA stagger like the
-// single-K kernel's jobs, hiding each pair's tracebacks under the other's
+// for that K and that item's labels.  Two or more pairs per CTA stagger like
+// the single-K kernel's jobs, hiding each pair's tracebacks under another's
 // forward steps.  (A template on IO so that the body's `if constexpr`
 // branches are discarded.)
 template <class IO>
@@ -402,7 +403,7 @@ pair_kernel_mk(const IO io, int64_t n_tiles, int C, uint8_t* __restrict__ decisi
 {
     const int64_t n_pairs_all = (n_tiles + 1) >> 1;
     auto pair_index = [&](int64_t t) -> int64_t {
-        if (t >= kJobs) return n_pairs_all;
+        if (t >= kMaxCtaPairs) return n_pairs_all;
         const int q = io.cta_pair[blockIdx.x][t];
         return q < 0 ? n_pairs_all : (int64_t)q;
     };
@@ -614,47 +615,44 @@ extern "C" int kq_ldlq_chain_step(const kq_chain_item* items, int n_items, int t
         set_error("kq_ldlq_chain_step: items of different K need even item starts");
         return KQ_ERR_ARG;
     }
-    // Per-CTA pair table.  At most one pair per SM: one pair per CTA.  More:
-    // the pairs of each (K, label table) two to a CTA (one when that group's
-    // count is odd), so every CTA runs one K and one codebook.
+    // Per-CTA pair table: the pairs of each (K, label table) group in runs of
+    // m to a CTA, m the smallest count (from ceil(pairs / SMs) up to
+    // kMaxCtaPairs) whose runs fit one CTA per SM, so every CTA runs one K and
+    // one codebook.  At most one pair per SM gives one pair per CTA.
     const int64_t pairs = (total + 1) / 2;
-    int ctas = 0;
-    if (pairs <= sms) {
-        for (int64_t p = 0; p < pairs; ++p) {
-            io.cta_pair[p][0] = (int16_t)p;
-            io.cta_pair[p][1] = -1;
-        }
-        ctas = (int)pairs;
+    int64_t gp[KQ_CHAIN_MAX_ITEMS] = {};      // pairs of the group led by item g (0: not a leader)
+    int leader[KQ_CHAIN_MAX_ITEMS];
+    for (int i = 0; i < n_items; ++i) {
+        leader[i] = i;
+        for (int g = 0; g < i; ++g)
+            if (leader[g] == g && items[g].K == items[i].K && items[g].labels == items[i].labels) { leader[i] = g; break; }
+        gp[leader[i]] += (io.start[i + 1] + 1) / 2 - io.start[i] / 2;
     }
-    bool grouped[KQ_CHAIN_MAX_ITEMS] = {};
-    for (int g = 0; g < n_items && pairs > sms && ctas <= sms; ++g) {
-        if (grouped[g]) continue;
-        int64_t q0 = -1;
-        for (int i = g; i < n_items && ctas <= sms; ++i) {
-            if (grouped[i] || items[i].K != items[g].K || items[i].labels != items[g].labels) continue;
-            grouped[i] = true;
-            for (int64_t p = io.start[i] / 2; p < (io.start[i + 1] + 1) / 2; ++p) {
-                if (q0 < 0) { q0 = p; continue; }
-                if (ctas < sms) {
-                    io.cta_pair[ctas][0] = (int16_t)q0;
-                    io.cta_pair[ctas][1] = (int16_t)p;
-                }
-                ++ctas;
-                q0 = -1;
-            }
-        }
-        if (q0 >= 0) {
-            if (ctas < sms) {
-                io.cta_pair[ctas][0] = (int16_t)q0;
-                io.cta_pair[ctas][1] = -1;
-            }
-            ++ctas;
-        }
+    int m = (int)std::max<int64_t>(1, (pairs + sms - 1) / sms), ctas = 0;
+    for (; m <= kMaxCtaPairs; ++m) {
+        int64_t c = 0;
+        for (int g = 0; g < n_items; ++g) c += (gp[g] + m - 1) / m;
+        if (c <= sms) { ctas = (int)c; break; }
     }
-    if (ctas > sms || pairs > 0x7FFF) {
-        set_error("kq_ldlq_chain_step: items of different K need at most 2 same-K tile pairs per SM (%lld pairs)",
-                  (long long)pairs);
+    if (m > kMaxCtaPairs || pairs > 0x7FFF) {
+        set_error("kq_ldlq_chain_step: items of different K need at most %d same-K tile pairs per SM (%lld pairs)",
+                  kMaxCtaPairs, (long long)pairs);
         return KQ_ERR_ARG;
+    }
+    {
+        int cta = 0, fill = 0;
+        for (int g = 0; g < n_items; ++g) {
+            if (leader[g] != g) continue;
+            for (int i = g; i < n_items; ++i) {
+                if (leader[i] != g) continue;
+                for (int64_t p = io.start[i] / 2; p < (io.start[i + 1] + 1) / 2; ++p) {
+                    if (fill == 0) for (int t = 0; t < kMaxCtaPairs; ++t) io.cta_pair[cta][t] = -1;
+                    io.cta_pair[cta][fill] = (int16_t)p;
+                    if (++fill == m) { fill = 0; ++cta; }
+                }
+            }
+            if (fill) { fill = 0; ++cta; }
+        }
     }
     if (max_ctas > 0 && ctas > max_ctas) {
         set_error("kq_ldlq_chain_step: a mixed-K launch needs %d CTAs (max_ctas %d)", ctas, max_ctas);

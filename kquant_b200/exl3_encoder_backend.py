@@ -1934,19 +1934,21 @@ def _launch_key(c: _Chain):
     return c.K, c.m.labels[c.K].data_ptr()
 
 
-def _launch_ctas(chains) -> int:
-    """CTAs of a mixed chain launch: one per tile pair up to one pair per SM; beyond, the pairs of each
-    (K, label table), two to a CTA (kq_ldlq_chain_step)."""
+MAX_CTA_PAIRS = 4   # tile pairs per CTA of one chain launch
+
+
+def _launch_fits(chains, sms: int) -> bool:
+    """Whether a mixed chain launch fits (kq_ldlq_chain_step): each (K, label table) group's tile pairs in runs
+    of m per CTA, m from ceil(pairs / SMs) up to MAX_CTA_PAIRS, need at most one CTA per SM."""
     pairs: dict = {}
     for c in chains:
         k = _launch_key(c)
         pairs[k] = pairs.get(k, 0) + (c.n_tiles + 1) // 2
-    return sum(pairs.values()), sum((p + 1) // 2 for p in pairs.values())
-
-
-def _launch_fits(chains, sms: int) -> bool:
-    pairs, doubled = _launch_ctas(chains)
-    return pairs <= sms or doubled <= sms
+    total = sum(pairs.values())
+    for m in range(max(1, -(-total // sms)), MAX_CTA_PAIRS + 1):
+        if sum(-(-p // m) for p in pairs.values()) <= sms:
+            return True
+    return False
 
 
 def _select_launch(cands: list, cap: int, sms: int) -> list:
@@ -2034,8 +2036,9 @@ def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None
     advances a set of chains by one 16-row step: the chains with the most
     steps left first (the critical path), then any others that fit, all with
     the same tail-biting context; chains of different K share launches.  A
-    launch holds up to 4 x SMs tiles (two tile pairs per CTA) while the work
-    left exceeds one wave per critical-path step, then up to 2 x SMs.  The kernel computes each step's feedback
+    launch holds up to 2 p x SMs tiles (p tile pairs per CTA, p up to 4) while
+    the work left exceeds what p - 1 pairs per SM along the critical path
+    would cover; one wave (2 x SMs) at the end.  The kernel computes each step's feedback
     product itself; the buffer-end feedback updates run between launches on
     the same stream.  ``on_buffer(chain)``, when given, is called when a chain
     is about to start a new 128-row buffer and may return replacement chains
@@ -2073,11 +2076,20 @@ def _chain_traverse(members: list, device: torch.device, chain_tiles: int | None
         # other's forward steps) while the remaining work exceeds what one-wave
         # launches along the critical path would cover; one pair per SM after.
         work = sum(c.n_tiles * c.remaining for c in same)
-        cap = (4 if work > 2 * sms * same[0].remaining else 2) * sms
-        sel = _select_launch(same, cap, sms)
-        if cap > 2 * sms and sum(c.n_tiles for c in sel) < 3.6 * sms:
-            # a launch of two pairs per SM pays only when nearly full
-            sel = _select_launch(same, 2 * sms, sms)
+        crit = same[0].remaining
+        # p tile pairs per SM: the largest p whose launches along the critical path
+        # would still not cover the work left; a launch of p > 1 pairs per SM
+        # pays only when it comes out at least 90% full.
+        p = 1
+        while p < MAX_CTA_PAIRS and work > 2 * sms * (p + 1) * crit:
+            p += 1
+        if p == 1 and work > 2 * sms * crit:
+            p = 2
+        while True:
+            sel = _select_launch(same, 2 * p * sms, sms)
+            if p == 1 or sum(c.n_tiles for c in sel) >= 0.9 * 2 * p * sms:
+                break
+            p -= 1
         _native.ldlq_chain_step([c.item() for c in sel], ctx, device)
         for c in sel:
             c.advance()

@@ -312,7 +312,7 @@ def test_mixed_chain_engine_odd_runs(cuda_device):
     assert torch.equal(wq_c, wq_o)
 
 
-@pytest.mark.parametrize("rates", [(3, 3, 3, 3, 3), (2, 3, 4, 3, 2)])
+@pytest.mark.parametrize("rates", [(3, 3, 3, 3, 3), (2, 3, 4, 3, 2), (2, 3, 4, 3, 2, 4, 3, 2, 3, 4)])
 def test_double_wave_chain_launches_equal_single_wave(cuda_device, monkeypatch, rates):
     """Launches of two tile pairs per CTA (uniform K: the grid-stride kernel; mixed K: the per-CTA pair table)
     give the same codes and What, bit for bit, as one-wave launches of the same chains."""
