@@ -942,14 +942,22 @@ def run_encode(args, world, rank, local):
 
 def run_layer_case(args, world, rank, local):
     """The whole layer once: 384 routed experts + the shared expert over the ranks (48 + 1 at 8 GPUs), encoded
-    in batches of --experts; reports the wall time (device events, max over ranks) and Mweights/s."""
+    in batches of --experts; reports the wall time (device events, max over ranks) and Mweights/s.  With one
+    process and --layer-ranks N, that process encodes the last (longest) of the N shards alone: the ranks share
+    no data, so an N-GPU run's wall time is its slowest shard's."""
     from kquant_b200 import _native
     from kquant_b200.sharding import shard_experts
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     _native.load()
-    mine = shard_experts([1.0] * LAYER_EXPERTS, world, rank)
-    if rank == world - 1:
+    ranks = args.layer_ranks or world
+    if world not in (1, ranks):
+        raise SystemExit("--layer-ranks must equal the number of processes (or run one process)")
+    # one process standing in for rank ranks-1 of a ranks-GPU run: that shard only (it also holds the
+    # shared expert, so it is the longest); the layer's wall time on `ranks` GPUs is this shard's time
+    shard = rank if world == ranks else ranks - 1
+    mine = shard_experts([1.0] * LAYER_EXPERTS, ranks, shard)
+    if shard == ranks - 1:
         mine = mine + [SHARED]
     layer = Layer(device, mine)
     layer.encode(layer.experts[:1])            # warm-up: one expert
@@ -970,6 +978,7 @@ def run_layer_case(args, world, rank, local):
     if rank == 0:
         ks = [k for row in layer.rates for k in row]
         print(json.dumps({"case": "layer", "experts": LAYER_EXPERTS + 1, "weights": total, "n_gpus": world,
+                          "layer_ranks": ranks, "one_shard_on_one_gpu": world != ranks,
                           "experts_per_gpu": len(mine), "bpw_mean": sum(ks) / len(ks),
                           "wall_s": t, "mweights_per_s": total / t / 1e6,
                           "proxy_mean": float(gp.mean()), "proxy_max": float(gp.max()),
@@ -1067,6 +1076,8 @@ def main():
     ap.add_argument("--experts", type=int, default=4, help="slice: experts per GPU; layer: experts per batch")
     ap.add_argument("--top", type=int, default=25, help="profile case: kernels listed")
     ap.add_argument("--layers", type=int, default=8, help="stream case: consecutive layers")
+    ap.add_argument("--layer-ranks", type=int, default=0,
+                    help="layer case: GPUs the layer is sharded over; one process runs the last shard alone")
     args = ap.parse_args()
     if args.tiles is None:
         args.tiles = 1 << 20 if args.case == "microbench" else 1184
