@@ -727,24 +727,31 @@ def run_chain_case(args, local):
 
 
 def run_profile_case(args, local):
-    """Kernel list of one warm triplet step (torch.profiler / CUPTI device times): every launch of the step with
-    its device time, grouped by kernel, as a launch list without a replaying profiler."""
+    """Kernel list of one warm step of the default workload (torch.profiler / CUPTI device times): every launch
+    of the step with its device time, grouped by kernel, plus the step's wall time (CUDA events), so the
+    device-idle share is visible; a launch list without a replaying profiler."""
     from torch.profiler import ProfilerActivity, profile
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    hf, h13, h2 = make_triplet(device, seed=1234)
-    exl = [to_exl(w) for w in hf]
+    from kquant_b200 import _native
+    _native.load()
+    wl = SliceWorkload(args, 1, 0, device)
     for _ in range(max(args.warmup, 1)):
-        encode_triplet([w.clone() for w in exl], h13, h2, device)
+        wl.step()
     torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        encode_triplet([w.clone() for w in exl], h13, h2, device)
+        a.record()
+        wl.step()
+        b.record()
         torch.cuda.synchronize()
     rows = sorted(prof.key_averages(), key=lambda e: -e.device_time_total)
     total = sum(e.device_time_total for e in rows)
-    print(json.dumps({"case": "profile", "device_ms": total / 1e3, "kernels": [
-        {"name": e.key[:120], "launches": e.count, "ms": e.device_time_total / 1e3,
-         "share": e.device_time_total / total} for e in rows[:args.top]]}, indent=1))
+    wall = a.elapsed_time(b)
+    print(json.dumps({"case": "profile", "workload": wl.config["workload"], "step_ms": wall,
+                      "device_busy_ms": total / 1e3, "idle_share": 1 - total / 1e3 / wall, "kernels": [
+                          {"name": e.key[:120], "launches": e.count, "ms": e.device_time_total / 1e3,
+                           "share": e.device_time_total / total} for e in rows[:args.top]]}, indent=1))
 
 
 class SliceWorkload:
