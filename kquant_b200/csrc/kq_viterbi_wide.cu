@@ -25,7 +25,11 @@
 //     are selected (lane 0 nodes in the low 16 bits of a word, lane 1 nodes
 //     in the high 16 bits); NW words per thread per step, written coalesced.
 //   * Tracebacks stream the decision rows through shared memory with a
-//     double-buffered cp.async pipeline; one lane walks them.
+//     double-buffered cp.async pipeline; one lane walks them.  A tile's final
+//     traceback is instead walked one row per primer step of the CTA's next
+//     tile (decision rows in two areas, alternating by tile), so it hides
+//     under that primer's forward steps; only the CTA's last tile and the
+//     primer tracebacks stay exposed.
 #include "kq_viterbi_common.cuh"
 
 namespace kq {
@@ -99,8 +103,9 @@ struct WideMap {
 
 template <int K>
 __host__ __device__ constexpr size_t wide_smem_bytes() {
-    // costs [2][PADDED] half, tile [256] half, reduction [16] u32, end state
-    return (size_t)2 * WideMap<K>::PADDED * 2 + 256 * 2 + 16 * 4 + 16;
+    // costs [2][PADDED] half, tile [256] half, reduction [16] u32, end state and
+    // traceback hand-over [4] int, states of the previous tile [256] u16
+    return (size_t)2 * WideMap<K>::PADDED * 2 + 256 * 2 + 16 * 4 + 16 + 256 * 2;
 }
 
 // One forward step.  STEP0: 0 = costs from cprev, 1 = zero prior cost (the
@@ -258,11 +263,13 @@ wide_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
     __half* cost = reinterpret_cast<__half*>(smem);                           // [2][PADDED]
     __half* wsh = cost + 2 * M::PADDED;                                        // [256]
     uint32_t* red = reinterpret_cast<uint32_t*>(wsh + 256);                    // [16]
-    int* es_sh = reinterpret_cast<int*>(red + 16);                             // [1]
+    int* es_sh = reinterpret_cast<int*>(red + 16);                             // [4]
+    uint16_t* enc = reinterpret_cast<uint16_t*>(es_sh + 4);                    // [256] states of the tile in output
     uint8_t* stage = smem + ((wide_smem_bytes<K>() + 127) & ~(size_t)127);
-    uint16_t* enc = reinterpret_cast<uint16_t*>(wsh);                          // reuses wsh after the final pass
     const int tid = threadIdx.x;
-    uint32_t* dec = reinterpret_cast<uint32_t*>(decisions + (size_t)blockIdx.x * 256 * M::ROW_BYTES);
+    // Two decision areas of 256 rows, alternating by tile: the final traceback
+    // of a tile walks its rows while the next tile's primer writes the other area.
+    uint32_t* dec_base = reinterpret_cast<uint32_t*>(decisions + (size_t)blockIdx.x * 2 * 256 * M::ROW_BYTES);
 
     half2 L[M::NP][M::QT];
     {
@@ -282,13 +289,36 @@ wide_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
         }
     }
 
-    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    // Pending final traceback of the previous tile (walked by thread 0, one row
+    // per primer step of the current tile): its tile, node, row and decisions.
+    bool pend = false;
+    int64_t ptile = 0;
+    int pnode = 0, prow = -1;
+    const uint32_t* pdec = dec_base;
+    auto output = [&](int64_t t) {
+        if (tid < 256) {
+            const uint16_t sv = enc[tid];
+            states[t * 256 + tid] = sv;
+            vals[t * 256 + tid] = __half2float(labels16[sv]);
+        }
+    };
+    int parity = 0;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, parity ^= 1) {
+        uint32_t* dec = dec_base + (size_t)parity * 256 * M::ROW_WORDS;
         if (tid < 256) wsh[tid] = __float2half_rn(tiles[tile * 256 + tid]);
         __syncthreads();
         int par = 0;
         // primer: 2C steps from position 256 - C; decisions from step C on
         for (int i = 0; i < 2 * C; ++i) {
             const int ri = (i + 256 - C) & 255;
+            const bool walk = pend && tid == 0 && prow >= 0;
+            uint32_t tbw = 0;
+            int tsh = 0;
+            if (walk) {
+                int word;
+                M::locate(pnode, word, tsh);
+                tbw = __ldcg(pdec + (size_t)prow * M::ROW_WORDS + word);
+            }
             const half2 w2 = __half2half2(wsh[ri]);
             __half* cp = cost + par * M::PADDED;
             __half* cn = cost + (par ^ 1) * M::PADDED;
@@ -296,8 +326,25 @@ wide_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
             if (i == 0) wide_step<K, false, 1>(L, cp, cn, w2, 0, row, tid);
             else if (i < C) wide_step<K, false, 0>(L, cp, cn, w2, 0, row, tid);
             else wide_step<K, true, 0>(L, cp, cn, w2, 0, row, tid);
+            if (walk) {
+                const int d = (int)((tbw >> tsh) & (M::Q - 1));
+                enc[prow] = (uint16_t)((d << (16 - K)) | pnode);
+                pnode = (d << M::DSHIFT) | (pnode >> K);
+                --prow;
+            }
             par ^= 1;
             __syncthreads();
+        }
+        if (pend) {
+            // rows the primer did not cover (2C < 256), then the previous tile's output
+            if (tid == 0) { es_sh[1] = pnode; es_sh[2] = prow; }
+            __syncthreads();
+            const int left = es_sh[2] + 1;
+            if (left > 0) wide_traceback<K>(pdec, left - 1, left, es_sh[1], stage, stage_bytes, enc, tid);
+            __syncthreads();
+            output(ptile);
+            __syncthreads();
+            pend = false;
         }
         // argmin over the second-to-last primer step's costs, reference tie order
         {
@@ -335,14 +382,19 @@ wide_kernel(const float* __restrict__ tiles, int64_t n_tiles, const uint32_t* __
             par ^= 1;
             __syncthreads();
         }
-        wide_traceback<K>(dec, 255, 256, es, stage, stage_bytes, enc, tid);
-        __syncthreads();
-        if (tid < 256) {
-            const uint16_t sv = enc[tid];
-            states[tile * 256 + tid] = sv;
-            vals[tile * 256 + tid] = __half2float(labels16[sv]);
+        if (tile + gridDim.x < n_tiles) {
+            // hand the final traceback to the next tile's primer steps
+            pend = true;
+            ptile = tile;
+            pnode = es;
+            prow = 255;
+            pdec = dec;
+        } else {
+            wide_traceback<K>(dec, 255, 256, es, stage, stage_bytes, enc, tid);
+            __syncthreads();
+            output(tile);
+            __syncthreads();
         }
-        __syncthreads();
     }
 }
 
@@ -363,7 +415,7 @@ int wide_launch(const float* tiles, int64_t n, const uint16_t* labels, int C, fl
     if (int rc = sm_count(&sms)) return rc;
     int64_t grid = n < sms ? n : sms;
     if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-    const size_t per_cta = (size_t)256 * WideMap<K>::ROW_BYTES;
+    const size_t per_cta = (size_t)2 * 256 * WideMap<K>::ROW_BYTES;
     if (ws_bytes < (size_t)grid * per_cta) {
         const int64_t fit = (int64_t)(ws_bytes / per_cta);
         if (fit < 1) {
@@ -400,7 +452,7 @@ size_t wide_decision_bytes(int K, int64_t n, int sms) {
     case 4: row = WideMap<4>::ROW_BYTES; break;
     default: return 0;
     }
-    return (size_t)(grid > 0 ? grid : 1) * 256 * row;
+    return (size_t)(grid > 0 ? grid : 1) * 2 * 256 * row;
 }
 
 // K1 and K5..K8 in production; K2..K4 reachable here for cross-checks of this
