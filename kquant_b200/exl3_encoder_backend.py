@@ -1991,6 +1991,19 @@ def _member_step_gen(m: _ChainMember):
                                 tf32=m.tf32, state=(m.wq.unsqueeze(0), m.enc.unsqueeze(0), m.P.unsqueeze(0)))
 
 
+@lru_cache
+def _side_stream_cached(device: torch.device, i: int):
+    return torch.cuda.Stream(device=device)
+
+
+def _side_stream(device, i: int):
+    """The i-th side stream of a device, created once and reused."""
+    d = torch.device(device)
+    if d.index is None:
+        d = torch.device(d.type, torch.cuda.current_device())
+    return _side_stream_cached(d, i)
+
+
 def _members_steps(ms: list) -> None:
     """LDLQ of members at rates the chain kernel does not cover (K1, K5..K8): one launch per 16-row step.
 
@@ -2006,10 +2019,11 @@ def _members_steps(ms: list) -> None:
     if len(ms) == 1:
         _drive(_member_step_gen(ms[0]))
         return
-    cur = torch.cuda.current_stream(ms[0].W.device)
+    dev = ms[0].W.device
+    cur = torch.cuda.current_stream(dev)
     live = []
-    for m in ms:
-        st = torch.cuda.Stream(device=m.W.device)
+    for i, m in enumerate(ms):
+        st = _side_stream(dev, i)
         st.wait_stream(cur)
         with torch.cuda.stream(st):
             live.append((st, _member_step_gen(m)))
