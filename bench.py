@@ -562,6 +562,35 @@ def run_pack_case(args, local):
     print(json.dumps(out))
 
 
+def run_reconstruct_case(args, local):
+    """Row W: the original-basis reconstruction of the triplet's three matrices on the Walsh-Hadamard kernel
+    (HBM-bound: one read and one write of each matrix), against the matmul form (two fp32 block GEMMs and
+    two scalings, as kquant/exl3_encoder_backend.py:2211-2216 computes it)."""
+    from kquant_b200 import _native
+    from kquant_b200 import exl3_encoder_backend as be
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(3)
+    mats = [(torch.randn(s, generator=g, device=device), torch.randn(s[0], generator=g, device=device),
+             torch.randn(s[1], generator=g, device=device)) for s in ((HIDDEN, INTER), (HIDDEN, INTER),
+                                                                       (INTER, HIDDEN))]
+    peak, src = _hbm_peak()
+    byt = sum(w.numel() for w, _, _ in mats) * 8
+    t = _time(lambda: [_native.reconstruct_rotated(w, u, v) for w, u, v in mats], args.steps, args.warmup)
+
+    def matmul_form():
+        for w, u, v in mats:
+            x = be.preapply_had_l(w, 128)
+            x *= u.unsqueeze(1)
+            x = be.preapply_had_r(x, 128)
+            x *= v.unsqueeze(0)
+
+    tm = _time(matmul_form, args.steps, args.warmup)
+    print(json.dumps({"case": "reconstruct", "weights": sum(w.numel() for w, _, _ in mats), "bytes": byt,
+                      "ms": t * 1e3, "gbs": byt / t / 1e9, "frac_of_hbm": byt / t / 1e9 / peak, "peak_source": src,
+                      "matmul_form_ms": tm * 1e3}))
+
+
 def run_load_case(args, local):
     """bf16 HF -> fp32 EXL weight load of the triplet (gate, up, down), plain and with a row gather."""
     from kquant_b200 import _native
@@ -1074,7 +1103,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--case", default="slice",
                     choices=["slice", "triplet", "layer", "stream", "qsrt", "chain", "viterbi", "microbench", "mla", "trace",
-                             "pack", "load", "hessian", "profile"],
+                             "pack", "load", "hessian", "profile", "reconstruct"],
                     help="viterbi: only the tile kernel on --tiles random tiles (profiling case)")
     ap.add_argument("--tiles", type=int, default=None, help="viterbi: 1184; microbench: 1,048,576")
     ap.add_argument("--K", type=int, default=K_BITS)
@@ -1093,7 +1122,8 @@ def main():
     world, rank, local = _dist()
     cases = {"profile": run_profile_case, "chain": run_chain_case, "qsrt": run_qsrt_case,
              "viterbi": run_viterbi_case, "trace": run_trace_case, "pack": run_pack_case, "load": run_load_case,
-             "hessian": run_hessian_case, "microbench": run_microbench_case, "mla": run_mla_case}
+             "hessian": run_hessian_case, "microbench": run_microbench_case, "mla": run_mla_case,
+             "reconstruct": run_reconstruct_case}
     if args.case in cases:
         cases[args.case](args, local)
     elif args.impl == "reference":

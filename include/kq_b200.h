@@ -255,6 +255,18 @@ int kq_bf16_to_f32_transposed(const uint16_t* src, int64_t rows, int64_t cols, i
                               const int64_t* row_perm, float* dst, void* stream);
 
 /*
+ * Reconstruction of encoded weights in the original basis:
+ *     out = had_r(had_l(wq) * su[:, None]) * sv[None, :]
+ * wq, out [k x n] fp32 row-major (k, n multiples of 128; 16-byte aligned),
+ * su [k], sv [n] fp32; had_l / had_r are the 128-block Sylvester Hadamards
+ * normalised 1/sqrt(128).  Replaces the matmul-based reconstruction of
+ * kquant/exl3_encoder_backend.py:2211-2216 and :2492-2498 (fast
+ * Walsh-Hadamard transforms; equal up to fp32 rounding).
+ */
+int kq_reconstruct_rotated(const float* wq, const float* su, const float* sv, int64_t k, int64_t n, float* out,
+                           void* stream);
+
+/*
  * Roofline probe (no reference counterpart): launches blocks x threads
  * threads that each issue iters*128 independent __hfma2 instructions.  Time
  * it with events on `stream`: HFMA2 rate = blocks*threads*iters*128 / time.

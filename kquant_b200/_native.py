@@ -40,6 +40,7 @@ EXPORTED = (
     "kq_accumulate_hessian",
     "kq_ldlq_step_encode",
     "kq_ldlq_chain_step",
+    "kq_reconstruct_rotated",
 )
 
 KQ_CHAIN_MAX_ITEMS = 64
@@ -91,6 +92,7 @@ def load() -> ctypes.CDLL:
         L.kq_gemm_abt_tf32.argtypes = [P, P, P, I64, I64, I64, I64, ctypes.c_float, ctypes.c_float, P, P]
         L.kq_ldlq_step_encode.argtypes = [P, P, I64, I64, I64, I64, I, P, I, P, P, P, I, P, SZ, P]
         L.kq_ldlq_chain_step.argtypes = [P, I, I, I, P, SZ, P]
+        L.kq_reconstruct_rotated.argtypes = [P, P, P, I64, I64, P, P]
         L.kq_hessian_workspace_bytes.argtypes = [I64, I64, I]
         L.kq_hessian_workspace_bytes.restype = SZ
         L.kq_accumulate_hessian.argtypes = [P, P, I64, I64, I64, P, I64, I, P, SZ, P, P]
@@ -445,3 +447,19 @@ def ldlq_chain_step(items, tailbite_context: int, device: torch.device, max_ctas
             b.record()
             stats.events.append((a, b, tiles, int(tailbite_context)))
     stats.launches += 1
+
+
+def reconstruct_rotated(wq: torch.Tensor, su: torch.Tensor, sv: torch.Tensor) -> torch.Tensor:
+    """had_r(had_l(wq) * su) * sv with 128-blocks (row W), wq [k, n] fp32, su [k], sv [n]; a new tensor."""
+    _cuda(wq, "wq", torch.float32)
+    k, n = wq.shape
+    su = su.reshape(-1).to(torch.float32).contiguous()
+    sv = sv.reshape(-1).to(torch.float32).contiguous()
+    if su.numel() != k or sv.numel() != n:
+        raise ValueError("su must have k and sv n entries")
+    out = torch.empty_like(wq)
+    with torch.cuda.device(wq.device):
+        _check(load().kq_reconstruct_rotated(wq.data_ptr(), su.data_ptr(), sv.data_ptr(), k, n, out.data_ptr(),
+                                             _stream(wq.device)), "kq_reconstruct_rotated")
+    stats.launches += 1
+    return out

@@ -1357,12 +1357,14 @@ def _codebook_tensors(quant_args: dict) -> dict:
 
 
 def _reconstruct(wq: torch.Tensor, su: torch.Tensor, sv: torch.Tensor) -> torch.Tensor:
-    """Original-basis weight: had_r(had_l(What) * su) * sv."""
-    w = preapply_had_l(wq, had_k)
-    w *= su
-    w = preapply_had_r(w, had_n)
-    w *= sv
-    return w
+    """Original-basis weight had_r(had_l(What) * su) * sv (kquant/exl3_encoder_backend.py:2211-2216).
+
+    One pass over What on the Walsh-Hadamard kernel (``kq_reconstruct_rotated``,
+    k and n multiples of 128 as the encoder requires); the reconstruction is an output only
+    (it never feeds the codes), so fp32 rounding differences from the
+    reference's matmul form are within its 1e-3 reconstruction bound.
+    """
+    return _native.reconstruct_rotated(wq.contiguous(), su, sv)
 
 
 def quantize_qsrt(weight: torch.Tensor, H_data: dict, quant_args: dict, return_weight_q: bool,

@@ -353,7 +353,7 @@ def unpack_qsrt_trellis_edges(packed: PackedQSRTTrellis) -> torch.Tensor:
 def decode_qsrt_exl3_weight(packed: PackedQSRTTrellis, suh: torch.Tensor, svh: torch.Tensor, *,
                             codebook: str = SQG_XOR_CHEB_T12) -> torch.Tensor:
     """Decode a complete payload to the physical EXL-oriented [K, N] weight."""
-    from .exl3_encoder_backend import preapply_had_l, preapply_had_r, tensor_core_perm_i
+    from .exl3_encoder_backend import tensor_core_perm_i
     packed.validate()
     if codebook not in QSRT_CODEBOOKS:
         raise ValueError(f"unsupported QSRT codebook: {codebook}")
@@ -375,5 +375,4 @@ def decode_qsrt_exl3_weight(packed: PackedQSRTTrellis, suh: torch.Tensor, svh: t
             vals[:, sel] = lab[states[:, sel]]
     vals = vals[..., tensor_core_perm_i(dev)]
     w = vals.reshape(d.k_tiles, d.n_tiles, 16, 16).permute(0, 2, 1, 3).reshape(k, n)
-    w = preapply_had_l(w, 128) * suh.to(device=dev, dtype=torch.float32).unsqueeze(1)
-    return (preapply_had_r(w, 128) * svh.to(device=dev, dtype=torch.float32).unsqueeze(0)).contiguous()
+    return _native.reconstruct_rotated(w.contiguous(), suh.to(device=dev), svh.to(device=dev))
