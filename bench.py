@@ -777,7 +777,19 @@ def run_profile_case(args, local):
     rows = sorted(prof.key_averages(), key=lambda e: -e.device_time_total)
     total = sum(e.device_time_total for e in rows)
     wall = a.elapsed_time(b)
+    # the longest device-idle gaps between consecutive kernels (where the host held the GPU back)
+    evs = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                 if e.device_type.name == "CUDA" and e.time_range.end > e.time_range.start)
+    gaps, last_end, last_name = [], None, None
+    for st, en, name in evs:
+        if last_end is not None and st > last_end:
+            gaps.append((st - last_end, last_name[:60], name[:60]))
+        if last_end is None or en > last_end:
+            last_end, last_name = en, name
+    gaps.sort(reverse=True)
     print(json.dumps({"case": "profile", "workload": wl.config["workload"], "step_ms": wall,
+                      "gap_total_ms": sum(g for g, _, _ in gaps) / 1e3,
+                      "top_gaps_us": [[round(g, 1), x, y] for g, x, y in gaps[:12]],
                       "device_busy_ms": total / 1e3, "idle_share": 1 - total / 1e3 / wall, "kernels": [
                           {"name": e.key[:120], "launches": e.count, "ms": e.device_time_total / 1e3,
                            "share": e.device_time_total / total} for e in rows[:args.top]]}, indent=1))
